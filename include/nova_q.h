@@ -1,0 +1,201 @@
+/*
+ * nova_q.h -- C ABI of the B200 (sm_100a) quantized-inference path.
+ *
+ * This is the drop-in boundary for pplmx/nova's cuda::quantize subsystem.
+ * Every entry point takes plain pointers, sizes and a cudaStream_t, returns
+ * an nq_status_t, and is implemented by hand-written sm_100a CUDA kernels in
+ * libnova_q.so.  The C++ API of the reference (FP8GEMM, MinMaxCalibrator,
+ * quantize_f32_to_int8, ...) is provided as thin inline shims over these
+ * functions in include/nova/quantize/*.hpp.
+ *
+ * Each declaration names the reference interface it replaces
+ * (file:line relative to the pplmx/nova source tree).
+ *
+ * Conventions
+ *   - Device pointers unless stated otherwise.  The library never frees
+ *     caller memory.
+ *   - Asynchronous on `stream` unless stated otherwise.  Entry points that
+ *     return values to the host (compute_minmax, build_histogram) synchronise
+ *     `stream`, as the reference does.
+ *   - Errors: a non-zero status; nq_last_error() returns a thread-local
+ *     message for the last failing call on this thread.  The reference prints
+ *     launch errors to stderr and continues (e.g. int8_kernels.cu:214-217);
+ *     the C++ shims keep that behaviour where the reference had it.
+ *   - Format codes: NQ_E4M3 / NQ_E5M2 are OCP FP8 (E4M3FN max 448, E5M2 max
+ *     57344) encoded round-to-nearest-even with saturation; NQ_INT8 is
+ *     symmetric int8 clamped to [-127, 127].  The reference's own FP8 codec
+ *     (IEEE-like, max 240, Inf 0x7C, NaN 0x7D) is available bit-exactly
+ *     through the *_fp8e4m3 / *_fp8e5m2 entry points that mirror its API.
+ */
+#ifndef NOVA_Q_H
+#define NOVA_Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* nq_stream_t; /* identical to cudaStream_t */
+
+typedef enum {
+    NQ_SUCCESS = 0,
+    NQ_ERROR_INVALID_VALUE = 1,  /* null pointer, bad size or enum         */
+    NQ_ERROR_UNSUPPORTED = 2,    /* shape / alignment the path cannot take */
+    NQ_ERROR_CUDA = 3,           /* a CUDA runtime or driver call failed   */
+    NQ_ERROR_OUT_OF_MEMORY = 4,
+    NQ_ERROR_NO_DEVICE = 5,      /* no sm_100 device is current            */
+    NQ_ERROR_DEVICE_TIMEOUT = 6  /* a kernel's bounded wait ran out        */
+} nq_status_t;
+
+typedef enum { NQ_E4M3 = 0, NQ_E5M2 = 1, NQ_INT8 = 2 } nq_format_t;
+typedef enum { NQ_F32 = 0, NQ_BF16 = 1, NQ_S32 = 2 } nq_dtype_t;
+/* B operand layout of a GEMM: NQ_B_KN is K x N row-major (the layout of
+   FP8GEMM::forward, fp8_gemm.cu:81); NQ_B_NK is N x K row-major (a
+   "packed" weight, the layout of a torch Linear weight). */
+typedef enum { NQ_B_KN = 0, NQ_B_NK = 1 } nq_b_layout_t;
+
+/* ---- runtime ----------------------------------------------------------- */
+const char* nq_status_string(nq_status_t s);
+const char* nq_last_error(void);
+int nq_version(void);
+/* Reads (and with clear != 0 resets) the device-side error word of the
+   current device: bit 0 = a bounded wait in a kernel timed out. */
+nq_status_t nq_device_error_flags(uint32_t* flags, int clear);
+
+/* ---- FP8 element-wise, reference codec ------------------------------------
+ * Replace src/cuda/quantize/fp8_kernels.cu:29-40 / include/cuda/quantize/
+ * fp8_kernels.hpp:30-59.  Codes are bit-identical to FP8E4M3(float) /
+ * FP8E5M2(float) of include/cuda/quantize/fp8_types.hpp:64-97,147-189. */
+nq_status_t nq_quantize_f32_to_fp8e4m3(const float* src, uint8_t* dst, size_t n, nq_stream_t s);
+nq_status_t nq_quantize_f32_to_fp8e5m2(const float* src, uint8_t* dst, size_t n, nq_stream_t s);
+/* fp8_kernels.hpp:46 / :48 (dst = decode(src) * scale) */
+nq_status_t nq_dequantize_fp8e4m3_to_f32(const uint8_t* src, float* dst, size_t n, float scale,
+                                         nq_stream_t s);
+nq_status_t nq_dequantize_fp8e5m2_to_f32(const uint8_t* src, float* dst, size_t n, float scale,
+                                         nq_stream_t s);
+/* fp8_kernels.hpp:50-52: dst[b][i] = FP8E4M3(src[b][i] * scales[b]); the
+   pointer arrays, sizes and scales are device arrays, as in the reference. */
+nq_status_t nq_quantize_batched_f32_to_fp8e4m3(const float* const* src, uint8_t* const* dst,
+                                               int batch, const size_t* sizes,
+                                               const float* scales, nq_stream_t s);
+/* fp8_kernels.hpp:54-56: dst[b][i] = decode(src[b][i]) * scales[b] */
+nq_status_t nq_dequantize_batched_fp8e4m3_to_f32(const uint8_t* const* src, float* const* dst,
+                                                 int batch, const size_t* sizes,
+                                                 const float* scales, nq_stream_t s);
+
+/* ---- INT8 element-wise -------------------------------------------------------
+ * include/cuda/quantize/int8_kernels.hpp:51-55 (and the _async twin :63-67):
+ * sym q = clamp(rn(x/scale), +-127); asym q = clamp(rn((x-zp)/scale), +-127). */
+nq_status_t nq_quantize_f32_to_int8(const float* src, int8_t* dst, size_t n, float scale,
+                                    float zero_point, int symmetric, nq_stream_t s);
+/* int8_kernels.hpp:57-61: sym q*scale, asym (q+zp)*scale */
+nq_status_t nq_dequantize_int8_to_f32(const int8_t* src, float* dst, size_t n, float scale,
+                                      float zero_point, int symmetric, nq_stream_t s);
+/* int8_kernels.hpp:75-79 (int8_kernels.cu:171-194) */
+nq_status_t nq_quantize_f32_to_int8_with_calibration(const float* src, int8_t* dst, size_t n,
+                                                     float min_val, float max_val, nq_stream_t s);
+/* QuantizedTensor<int8_t>::FromFloat rounding (quantize_tensor.hpp:176-182):
+   q = clamp(round_half_away(x/scale), +-127). */
+nq_status_t nq_quantize_f32_to_int8_round_away(const float* src, int8_t* dst, size_t n,
+                                               float scale, nq_stream_t s);
+
+/* ---- reductions and calibration ----------------------------------------------
+ * int8_kernels.hpp:88-92 (int8_kernels.cu:324-410).  `data` may be host or
+ * device memory, as may `min_val` / `max_val`.  Synchronises `s`.  NaNs are
+ * ignored; n == 0 gives 0, 0. */
+nq_status_t nq_compute_minmax(const float* data, size_t n, float* min_val, float* max_val,
+                              nq_stream_t s);
+/* int8_kernels.hpp:81-86 (int8_kernels.cu:275-322).  `data` host or device,
+   `histogram` device with num_bins entries, zeroed here.  Synchronises `s`.
+   Unlike the reference kernel, any num_bins in [1, 65536] is counted
+   correctly (the reference kept only 256 shared bins). */
+nq_status_t nq_build_histogram(const float* data, uint32_t* histogram, size_t n, float min_val,
+                               float max_val, int num_bins, nq_stream_t s);
+
+/* Device-resident, asynchronous min/max: d_out[0] = min, d_out[1] = max. */
+nq_status_t nq_minmax_async(const float* data, size_t n, float* d_out, nq_stream_t s);
+/* amax of |x| and the per-tensor scale for `fmt`: d_out[0] = amax,
+   d_out[1] = amax / qmax (448, 57344 or 127), 1.0 when amax == 0.
+   src_dtype NQ_F32 or NQ_BF16. */
+nq_status_t nq_amax_scale_async(const void* data, nq_dtype_t src_dtype, size_t n,
+                                nq_format_t fmt, float* d_out, nq_stream_t s);
+/* Per-channel min/max of a rows x cols row-major matrix (one channel per
+   row, the layout PerChannelCalibrator::calibrate_per_channel walks,
+   calibrator.cpp:233-253) in one launch. */
+nq_status_t nq_minmax_rows(const float* data, int rows, int cols, float* d_min, float* d_max,
+                           nq_stream_t s);
+
+/* ---- scaled quantize (OCP FP8 / INT8, RNE, saturating) ---------------------
+ * q = encode(x / scale) with an IEEE division; `d_scale` is a device scalar
+ * (e.g. written by nq_amax_scale_async, no host round trip). */
+nq_status_t nq_quantize_scaled(const void* src, nq_dtype_t src_dtype, uint8_t* dst, size_t n,
+                               nq_format_t fmt, const float* d_scale, nq_stream_t s);
+/* dst = decode(q) * scale (f32 out) */
+nq_status_t nq_dequantize_scaled(const uint8_t* src, float* dst, size_t n, nq_format_t fmt,
+                                 const float* d_scale, nq_stream_t s);
+/* amax -> scale -> quantize, two launches, no host synchronisation.
+   d_amax_scale receives {amax, scale}. */
+nq_status_t nq_calibrate_quantize(const void* src, nq_dtype_t src_dtype, uint8_t* dst, size_t n,
+                                  nq_format_t fmt, float* d_amax_scale, nq_stream_t s);
+/* Per-row dynamic quantization (per token of activations, or per output
+   channel of an N x K weight): scales[r] = amax(row r)/qmax (1.0 for an
+   all-zero row), q = encode(x / scales[r]).  One launch. */
+nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst, float* scales,
+                             int rows, int cols, nq_format_t fmt, nq_stream_t s);
+/* Per-column scales of a rows x cols (K x N) row-major fp32 matrix: the
+   per-output-channel scales of a weight in FP8GEMM's B layout. */
+nq_status_t nq_quantize_cols(const float* src, uint8_t* dst, float* scales, int rows, int cols,
+                             nq_format_t fmt, nq_stream_t s);
+
+/* ---- GEMM -------------------------------------------------------------------
+ * out[m, n] = epi( sum_k A[m, k] * B[k, n] )
+ *   A: M x K row-major codes (K-major), B: per b_layout.
+ *   FP8 (a/b_format E4M3/E5M2, any mix): fp32 accumulation on tcgen05
+ *   kind::f8f6f4.  INT8 (both NQ_INT8): exact int32 accumulation on
+ *   tcgen05 kind::i8.
+ *   epi(acc) = ((acc * alpha) [* row_scale[m]]) [* col_scale[n]] [+ bias[n]],
+ *   each step one fp32 rounding, then converted to out_dtype (NQ_F32,
+ *   NQ_BF16 round-to-nearest-even, or NQ_S32 = raw int32 accumulators,
+ *   INT8 only).
+ * Shapes with K % 16, N % 16 or pointers not 16-byte aligned run a SIMT
+ * kernel with the same arithmetic. */
+typedef struct {
+    int m, n, k;
+    nq_format_t a_format, b_format;
+    nq_b_layout_t b_layout;
+    nq_dtype_t out_dtype;
+    float alpha;
+    const float* row_scale; /* [m] device, or NULL */
+    const float* col_scale; /* [n] device, or NULL */
+    const float* bias;      /* [n] device, or NULL */
+} nq_gemm_desc_t;
+
+nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out,
+                    nq_stream_t s);
+/* The same GEMM on the CUDA cores only (one thread per output, sequential-k
+   fp32 FMA or int32 accumulation): an exactly ordered variant for checking
+   and for shapes far below one tensor-core tile. */
+nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out,
+                         nq_stream_t s);
+
+/* FP8GEMM::forward / forward_async, include/cuda/quantize/fp8_gemm.hpp:55-69
+   (fp8_gemm.cu:164-198): fp32 out = scale_out * sum (a*scale_a)(b*scale_b),
+   A M x K, B K x N, E4M3 codes read as OCP E4M3FN by the tensor cores. */
+nq_status_t nq_fp8_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k,
+                                int n, float scale_a, float scale_b, float scale_out,
+                                nq_stream_t s);
+/* FP8E5M2GEMM::forward, fp8_gemm.hpp:101-107 (fp8_gemm.cu:232-258); the
+   operands are decoded as E5M2 (the reference reinterpreted them as E4M3). */
+nq_status_t nq_fp8e5m2_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k,
+                                    int n, float scale_a, float scale_b, float scale_out,
+                                    nq_stream_t s);
+/* FP8GEMM::get_workspace_size, fp8_gemm.cu:152-162 (same formula; the
+   kernels here need no workspace). */
+size_t nq_fp8_gemm_workspace_size(int m, int k, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NOVA_Q_H */

@@ -1,0 +1,424 @@
+// elementwise.cu -- quantize / dequantize kernels (HBM-bound).
+//
+// Every kernel streams its input with 128-bit loads and writes 128-bit
+// stores: one thread handles 16 elements per step (64 B of fp32 in and 16 B
+// of codes out for a quantize), on a grid-stride loop over a grid sized to the
+// SM count.  Tails (n % 16) and unaligned pointers take a scalar loop with the
+// same arithmetic, so the result never depends on the path.
+#include <algorithm>
+
+#include "codec.cuh"
+#include "nq_internal.h"
+
+namespace nq {
+namespace {
+
+using dev::Fmt;
+
+__device__ __forceinline__ bool dev_aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ---- vector load / store of 16 elements --------------------------------------
+__device__ __forceinline__ void load16(const float* p, float (&x)[16]) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float4 v = __ldg(q + i);
+        x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+    }
+}
+__device__ __forceinline__ void load16(const uint16_t* p, float (&x)[16]) {  // bf16 bits
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        uint4 v = __ldg(q + i);
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+            x[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        }
+    }
+}
+__device__ __forceinline__ float load1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float load1(const uint16_t* p) {
+    return __uint_as_float(static_cast<uint32_t>(__ldg(p)) << 16);
+}
+__device__ __forceinline__ void store16_codes(uint8_t* p, const uint32_t (&c)[16]) {
+    uint4 v;
+    v.x = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+    v.y = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+    v.z = c[8] | (c[9] << 8) | (c[10] << 16) | (c[11] << 24);
+    v.w = c[12] | (c[13] << 8) | (c[14] << 16) | (c[15] << 24);
+    *reinterpret_cast<uint4*>(p) = v;
+}
+__device__ __forceinline__ void load16_codes(const uint8_t* p, uint32_t (&c)[16]) {
+    uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) c[i] = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+}
+__device__ __forceinline__ void store16(float* p, const float (&y)[16]) {
+    float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+}
+
+// ---- element ops ---------------------------------------------------------------
+// Each op maps one input value to one output; quantize ops produce a code.
+struct CompatE4M3 {
+    __device__ uint32_t operator()(float x) const { return dev::compat_e4m3_encode(x); }
+};
+struct CompatE5M2 {
+    __device__ uint32_t operator()(float x) const { return dev::compat_e5m2_encode(x); }
+};
+// int8_kernels.cu:29-35: IEEE division (no fast math), RNE, clamp +-127
+struct Int8Sym {
+    float scale;
+    __device__ uint32_t operator()(float x) const { return dev::int8_encode(x / scale); }
+};
+struct Int8Asym {
+    float scale, zp;
+    __device__ uint32_t operator()(float x) const { return dev::int8_encode((x - zp) / scale); }
+};
+// int8_kernels.cu:182-193: s = range/254, q = rn((x - min)/s - 127), 0 if range < 1e-6
+struct Int8Calib {
+    float min_val, range;
+    __device__ uint32_t operator()(float x) const {
+        if (range < 1e-6f) return 0u;
+        const float s = range / 254.0f;
+        return dev::int8_encode(__fsub_rn((x - min_val) / s, 127.0f));
+    }
+};
+// quantize_tensor.hpp:176-182: std::round (half away from zero), clamp +-127
+struct Int8RoundAway {
+    float scale;
+    __device__ uint32_t operator()(float x) const {
+        float r = roundf(x / scale);
+        r = fmaxf(-127.0f, fminf(127.0f, r));
+        return static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu;
+    }
+};
+
+template <class Op, class In>
+__global__ void __launch_bounds__(256) k_quant(const In* __restrict__ src, uint8_t* __restrict__ dst,
+                                               size_t n, int vec, Op op) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        float x[16];
+        load16(src + v * 16, x);
+        uint32_t c[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[i] = op(x[i]);
+        store16_codes(dst + v * 16, c);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride) dst[i] = static_cast<uint8_t>(op(load1(src + i)));
+}
+
+// Scaled OCP / INT8 quantize, the scale read from device memory.
+template <int F, class In>
+__global__ void __launch_bounds__(256) k_quant_scaled(const In* __restrict__ src,
+                                                      uint8_t* __restrict__ dst, size_t n, int vec,
+                                                      const float* __restrict__ d_scale) {
+    const float s = __ldg(d_scale);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        float x[16];
+        load16(src + v * 16, x);
+        uint32_t c[16];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+            uint32_t p = dev::ocp_encode2<F>(x[i] / s, x[i + 1] / s);
+            c[i] = p & 0xFFu;
+            c[i + 1] = p >> 8;
+        }
+        store16_codes(dst + v * 16, c);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride)
+        dst[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(load1(src + i) / s, 0.0f) & 0xFFu);
+}
+
+// ---- dequantize ---------------------------------------------------------------
+struct DecCompatE4M3 {
+    float scale;
+    __device__ float operator()(uint32_t c) const { return dev::compat_e4m3_decode(c) * scale; }
+};
+struct DecCompatE5M2 {
+    float scale;
+    __device__ float operator()(uint32_t c) const { return dev::compat_e5m2_decode(c) * scale; }
+};
+// int8_kernels.cu:53-57
+struct DecInt8Sym {
+    float scale;
+    __device__ float operator()(uint32_t c) const {
+        return static_cast<float>(static_cast<int8_t>(c)) * scale;
+    }
+};
+struct DecInt8Asym {
+    float scale, zp;
+    __device__ float operator()(uint32_t c) const {
+        return __fmul_rn(__fadd_rn(static_cast<float>(static_cast<int8_t>(c)), zp), scale);
+    }
+};
+template <int F>
+struct DecOcp {
+    float scale;
+    __device__ float operator()(uint32_t c) const { return dev::ocp_decode2<F>(c).x * scale; }
+};
+
+template <class Op>
+__global__ void __launch_bounds__(256) k_dequant(const uint8_t* __restrict__ src,
+                                                 float* __restrict__ dst, size_t n, int vec, Op op) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        uint32_t c[16];
+        load16_codes(src + v * 16, c);
+        float y[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) y[i] = op(c[i]);
+        store16(dst + v * 16, y);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride) dst[i] = op(__ldg(src + i));
+}
+
+template <class Op>
+__global__ void __launch_bounds__(256) k_dequant_scaled(const uint8_t* __restrict__ src,
+                                                        float* __restrict__ dst, size_t n, int vec,
+                                                        const float* __restrict__ d_scale) {
+    Op op{__ldg(d_scale)};
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        uint32_t c[16];
+        load16_codes(src + v * 16, c);
+        float y[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) y[i] = op(c[i]);
+        store16(dst + v * 16, y);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride) dst[i] = op(__ldg(src + i));
+}
+
+// ---- batched (fp8_kernels.cu:83-122): grid.y = tensor, grid.x strides ------------
+__global__ void __launch_bounds__(256) k_quant_batched(const float* const* src, uint8_t* const* dst,
+                                                       const size_t* sizes, const float* scales) {
+    const int b = blockIdx.y;
+    const float* s = src[b];
+    uint8_t* d = dst[b];
+    const size_t n = sizes[b];
+    const float mul = scales[b];
+    const bool vec = dev_aligned16(s) && dev_aligned16(d);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        float x[16];
+        load16(s + v * 16, x);
+        uint32_t c[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[i] = dev::compat_e4m3_encode(x[i] * mul);
+        store16_codes(d + v * 16, c);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride)
+        d[i] = static_cast<uint8_t>(dev::compat_e4m3_encode(__ldg(s + i) * mul));
+}
+
+__global__ void __launch_bounds__(256) k_dequant_batched(const uint8_t* const* src, float* const* dst,
+                                                         const size_t* sizes, const float* scales) {
+    const int b = blockIdx.y;
+    const uint8_t* s = src[b];
+    float* d = dst[b];
+    const size_t n = sizes[b];
+    const float mul = scales[b];
+    const bool vec = dev_aligned16(s) && dev_aligned16(d);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        uint32_t c[16];
+        load16_codes(s + v * 16, c);
+        float y[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) y[i] = dev::compat_e4m3_decode(c[i]) * mul;
+        store16(d + v * 16, y);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride) d[i] = dev::compat_e4m3_decode(__ldg(s + i)) * mul;
+}
+
+// ---- launch helpers ------------------------------------------------------------------
+nq_status_t grid_for(size_t n, int* grid) {
+    DeviceInfo di;
+    nq_status_t st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    const size_t work = (n + 15) / 16;
+    const size_t want = (work + 255) / 256;
+    const size_t cap = static_cast<size_t>(di.sm_count) * 8;  // 8 x 256 threads per SM
+    *grid = static_cast<int>(std::max<size_t>(1, std::min(want, cap)));
+    return NQ_SUCCESS;
+}
+
+template <class Op, class In>
+nq_status_t launch_quant(const In* src, uint8_t* dst, size_t n, Op op, cudaStream_t s, const char* what) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst) return fail(NQ_ERROR_INVALID_VALUE, std::string(what) + ": null pointer");
+    int grid;
+    nq_status_t st = grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    const int vec = aligned16(src) && aligned16(dst);
+    k_quant<Op, In><<<grid, 256, 0, s>>>(src, dst, n, vec, op);
+    NQ_LAUNCH_CHECK(what);
+    return NQ_SUCCESS;
+}
+
+template <class Op>
+nq_status_t launch_dequant(const uint8_t* src, float* dst, size_t n, Op op, cudaStream_t s, const char* what) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst) return fail(NQ_ERROR_INVALID_VALUE, std::string(what) + ": null pointer");
+    int grid;
+    nq_status_t st = grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    const int vec = aligned16(src) && aligned16(dst);
+    k_dequant<Op><<<grid, 256, 0, s>>>(src, dst, n, vec, op);
+    NQ_LAUNCH_CHECK(what);
+    return NQ_SUCCESS;
+}
+
+template <int F>
+nq_status_t launch_quant_scaled(const void* src, nq_dtype_t dt, uint8_t* dst, size_t n,
+                                const float* d_scale, cudaStream_t s, int grid) {
+    const int vec = aligned16(src) && aligned16(dst);
+    if (dt == NQ_F32)
+        k_quant_scaled<F, float><<<grid, 256, 0, s>>>(static_cast<const float*>(src), dst, n, vec, d_scale);
+    else
+        k_quant_scaled<F, uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(src), dst, n, vec,
+                                                         d_scale);
+    NQ_LAUNCH_CHECK("nq_quantize_scaled");
+    return NQ_SUCCESS;
+}
+
+}  // namespace
+
+// Used by reduce.cu's calibrate+quantize pipeline.
+nq_status_t quantize_scaled_impl(const void* src, nq_dtype_t dt, uint8_t* dst, size_t n, nq_format_t fmt,
+                                 const float* d_scale, cudaStream_t s) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst || !d_scale) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_scaled: null pointer");
+    if (dt != NQ_F32 && dt != NQ_BF16) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_scaled: src dtype");
+    int grid;
+    nq_status_t st = grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    switch (fmt) {
+        case NQ_E4M3: return launch_quant_scaled<dev::kE4M3>(src, dt, dst, n, d_scale, s, grid);
+        case NQ_E5M2: return launch_quant_scaled<dev::kE5M2>(src, dt, dst, n, d_scale, s, grid);
+        case NQ_INT8: return launch_quant_scaled<dev::kINT8>(src, dt, dst, n, d_scale, s, grid);
+    }
+    return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_scaled: format");
+}
+
+}  // namespace nq
+
+using nq::fail;
+
+extern "C" {
+
+nq_status_t nq_quantize_f32_to_fp8e4m3(const float* src, uint8_t* dst, size_t n, nq_stream_t s) {
+    return nq::launch_quant(src, dst, n, nq::CompatE4M3{}, s, "nq_quantize_f32_to_fp8e4m3");
+}
+nq_status_t nq_quantize_f32_to_fp8e5m2(const float* src, uint8_t* dst, size_t n, nq_stream_t s) {
+    return nq::launch_quant(src, dst, n, nq::CompatE5M2{}, s, "nq_quantize_f32_to_fp8e5m2");
+}
+nq_status_t nq_dequantize_fp8e4m3_to_f32(const uint8_t* src, float* dst, size_t n, float scale,
+                                         nq_stream_t s) {
+    return nq::launch_dequant(src, dst, n, nq::DecCompatE4M3{scale}, s, "nq_dequantize_fp8e4m3_to_f32");
+}
+nq_status_t nq_dequantize_fp8e5m2_to_f32(const uint8_t* src, float* dst, size_t n, float scale,
+                                         nq_stream_t s) {
+    return nq::launch_dequant(src, dst, n, nq::DecCompatE5M2{scale}, s, "nq_dequantize_fp8e5m2_to_f32");
+}
+
+nq_status_t nq_quantize_batched_f32_to_fp8e4m3(const float* const* src, uint8_t* const* dst, int batch,
+                                               const size_t* sizes, const float* scales, nq_stream_t s) {
+    if (batch == 0) return NQ_SUCCESS;
+    if (batch < 0 || batch > 65535 || !src || !dst || !sizes || !scales)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_batched_f32_to_fp8e4m3: bad arguments");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    dim3 grid(std::max(1, di.sm_count * 8 / batch), batch);
+    nq::k_quant_batched<<<grid, 256, 0, s>>>(src, dst, sizes, scales);
+    NQ_LAUNCH_CHECK("nq_quantize_batched_f32_to_fp8e4m3");
+    return NQ_SUCCESS;
+}
+
+nq_status_t nq_dequantize_batched_fp8e4m3_to_f32(const uint8_t* const* src, float* const* dst, int batch,
+                                                 const size_t* sizes, const float* scales, nq_stream_t s) {
+    if (batch == 0) return NQ_SUCCESS;
+    if (batch < 0 || batch > 65535 || !src || !dst || !sizes || !scales)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_dequantize_batched_fp8e4m3_to_f32: bad arguments");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    dim3 grid(std::max(1, di.sm_count * 8 / batch), batch);
+    nq::k_dequant_batched<<<grid, 256, 0, s>>>(src, dst, sizes, scales);
+    NQ_LAUNCH_CHECK("nq_dequantize_batched_fp8e4m3_to_f32");
+    return NQ_SUCCESS;
+}
+
+nq_status_t nq_quantize_f32_to_int8(const float* src, int8_t* dst, size_t n, float scale, float zero_point,
+                                    int symmetric, nq_stream_t s) {
+    uint8_t* d = reinterpret_cast<uint8_t*>(dst);
+    if (symmetric) return nq::launch_quant(src, d, n, nq::Int8Sym{scale}, s, "nq_quantize_f32_to_int8");
+    return nq::launch_quant(src, d, n, nq::Int8Asym{scale, zero_point}, s, "nq_quantize_f32_to_int8");
+}
+
+nq_status_t nq_dequantize_int8_to_f32(const int8_t* src, float* dst, size_t n, float scale, float zero_point,
+                                      int symmetric, nq_stream_t s) {
+    const uint8_t* q = reinterpret_cast<const uint8_t*>(src);
+    if (symmetric) return nq::launch_dequant(q, dst, n, nq::DecInt8Sym{scale}, s, "nq_dequantize_int8_to_f32");
+    return nq::launch_dequant(q, dst, n, nq::DecInt8Asym{scale, zero_point}, s, "nq_dequantize_int8_to_f32");
+}
+
+nq_status_t nq_quantize_f32_to_int8_with_calibration(const float* src, int8_t* dst, size_t n, float min_val,
+                                                     float max_val, nq_stream_t s) {
+    return nq::launch_quant(src, reinterpret_cast<uint8_t*>(dst), n, nq::Int8Calib{min_val, max_val - min_val}, s,
+                            "nq_quantize_f32_to_int8_with_calibration");
+}
+
+nq_status_t nq_quantize_f32_to_int8_round_away(const float* src, int8_t* dst, size_t n, float scale,
+                                               nq_stream_t s) {
+    return nq::launch_quant(src, reinterpret_cast<uint8_t*>(dst), n, nq::Int8RoundAway{scale}, s,
+                            "nq_quantize_f32_to_int8_round_away");
+}
+
+nq_status_t nq_quantize_scaled(const void* src, nq_dtype_t src_dtype, uint8_t* dst, size_t n, nq_format_t fmt,
+                               const float* d_scale, nq_stream_t s) {
+    return nq::quantize_scaled_impl(src, src_dtype, dst, n, fmt, d_scale, s);
+}
+
+nq_status_t nq_dequantize_scaled(const uint8_t* src, float* dst, size_t n, nq_format_t fmt, const float* d_scale,
+                                 nq_stream_t s) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst || !d_scale) return fail(NQ_ERROR_INVALID_VALUE, "nq_dequantize_scaled: null pointer");
+    int grid;
+    nq_status_t st = nq::grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    const int vec = nq::aligned16(src) && nq::aligned16(dst);
+    switch (fmt) {
+        case NQ_E4M3: nq::k_dequant_scaled<nq::DecOcp<nq::dev::kE4M3>><<<grid, 256, 0, s>>>(src, dst, n, vec, d_scale); break;
+        case NQ_E5M2: nq::k_dequant_scaled<nq::DecOcp<nq::dev::kE5M2>><<<grid, 256, 0, s>>>(src, dst, n, vec, d_scale); break;
+        case NQ_INT8: nq::k_dequant_scaled<nq::DecInt8Sym><<<grid, 256, 0, s>>>(src, dst, n, vec, d_scale); break;
+        default: return fail(NQ_ERROR_INVALID_VALUE, "nq_dequantize_scaled: format");
+    }
+    NQ_LAUNCH_CHECK("nq_dequantize_scaled");
+    return NQ_SUCCESS;
+}
+
+}  // extern "C"

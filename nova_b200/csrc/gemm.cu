@@ -1,0 +1,462 @@
+// gemm.cu -- FP8 (kind::f8f6f4) and INT8 (kind::i8) GEMMs on the sm_100a
+// tensor cores, with the scale / bias / bf16 epilogue fused.
+//
+// Kernel k_gemm_tc (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile [128 x 128 B] and B tile [128 B x 256]
+//               per stage, 128-byte swizzle, 4-stage ring of 48 KB stages.
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32/s32
+//               accumulators) and one elected thread issues tcgen05.mma
+//               (M=128, N=256, K=32 per instruction, 4 per stage), committing
+//               each stage back to the producer and each finished tile to the
+//               epilogue.
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output rows),
+//               acc * alpha [* row_scale] [* col_scale] [+ bias], convert,
+//               store; then hand the accumulator back, so the MMA of tile i+1
+//               overlaps the epilogue of tile i.
+// B is read either K x N row-major (FP8GEMM::forward's layout, the MN-major
+// operand form of tcgen05) or N x K row-major (K-major, a packed weight).
+// Every wait is bounded (ptx.cuh); a timeout sets the device error word.
+//
+// Kernel k_gemm_simt: one thread per output, sequential-k FMA (int32 for
+// INT8), for shapes the TMA path cannot take (K or N not a multiple of 16,
+// unaligned pointers) and tiny problems.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "codec.cuh"
+#include "nq_internal.h"
+#include "ptx.cuh"
+
+namespace nq {
+namespace {
+
+using namespace dev;
+
+constexpr int BM = 128, BN = 256, BK = 128;  // BK in elements (= bytes)
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK;        // 16 KB
+constexpr int B_STAGE = BN * BK;        // 32 KB
+constexpr int TMEM_COLS = 2 * BN;       // two accumulators
+constexpr int GEMM_THREADS = 192;
+constexpr int SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+
+struct Epi {
+    void* out;
+    int ldo;  // elements per output row
+    nq_dtype_t out_dtype;
+    float alpha;
+    const float* row_scale;
+    const float* col_scale;
+    const float* bias;
+};
+
+// v = ((acc * alpha) [* rs]) [* cs] [+ b]: one rounding per step, never fused.
+__device__ __forceinline__ float epi_value(float acc, float alpha, float rs, const float* col_scale,
+                                           const float* bias, int col) {
+    float v = __fmul_rn(acc, alpha);
+    if (rs != 1.0f) v = __fmul_rn(v, rs);
+    if (col_scale) v = __fmul_rn(v, __ldg(col_scale + col));
+    if (bias) v = __fadd_rn(v, __ldg(bias + col));
+    return v;
+}
+
+template <bool INT_ACC>
+__device__ __forceinline__ void store_chunk(const Epi& ep, const uint32_t (&r)[32], int row, int col0, int N,
+                                            float rs) {
+    if (INT_ACC && ep.out_dtype == NQ_S32) {
+        int32_t* o = static_cast<int32_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
+        if (col0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<int4*>(o + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        } else {
+            for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = static_cast<int32_t>(r[j]);
+        }
+        return;
+    }
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float acc = INT_ACC ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+        const int col = min(col0 + j, N - 1);  // columns past N are computed but never stored
+        v[j] = epi_value(acc, ep.alpha, rs, ep.col_scale, ep.bias, col);
+    }
+    if (ep.out_dtype == NQ_BF16) {
+        uint16_t* o = static_cast<uint16_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
+        if (col0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 w;
+                w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
+                w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
+                w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
+                w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
+                *reinterpret_cast<uint4*>(o + j) = w;
+            }
+        } else {
+            for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = static_cast<uint16_t>(f32x2_to_bf16x2(v[j], 0.0f));
+        }
+    } else {
+        float* o = static_cast<float*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
+        if (col0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+            for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = v[j];
+        }
+    }
+}
+
+template <bool INT8_KIND, bool B_KN>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+              uint32_t idesc, Epi ep, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
+    uint64_t* full = bars;                // [STAGES] TMA -> MMA
+    uint64_t* empty = bars + STAGES;      // [STAGES] MMA -> TMA
+    uint64_t* tfull = bars + 2 * STAGES;  // [2] MMA -> epilogue
+    uint64_t* tempty = tfull + 2;         // [2] epilogue -> MMA
+    uint64_t* done = tempty + 2;          // MMA drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m_tiles = (M + BM - 1) / BM;
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = m_tiles * n_tiles;
+    const int kblocks = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int mb = tile % m_tiles, nb = tile / m_tiles;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[stage], A_STAGE + B_STAGE);
+                    tma_load_2d(sA + stage * A_STAGE, &tmA, &full[stage], kb * BK, mb * BM);
+                    if (B_KN) {
+                        tma_load_2d(sB + stage * B_STAGE, &tmB, &full[stage], nb * BN, kb * BK);
+                        tma_load_2d(sB + stage * B_STAGE + B_STAGE / 2, &tmB, &full[stage], nb * BN + BN / 2, kb * BK);
+                    } else {
+                        tma_load_2d(sB + stage * B_STAGE, &tmB, &full[stage], kb * BK, nb * BN);
+                    }
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // Let the copies already issued land before the CTA can exit.
+                for (int s = 0; s < STAGES; ++s) {
+                    int st = stage - 1 - s;
+                    uint32_t ph = phase;
+                    if (st < 0) { st += STAGES; ph ^= 1u; }
+                    mbar_wait(&full[st], ph, nullptr);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+                const int acc = it & 1;
+                const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + stage * A_STAGE);
+                    const uint32_t b_addr = smem_u32(sB + stage * B_STAGE);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk) {
+                        // A: K-major, 128-byte rows, 8-row groups 1024 B apart;
+                        //    the k-th 32-byte slice starts 32*kk bytes in.
+                        const uint64_t adesc = smem_desc_sw128(a_addr + 32u * kk, 16u, 1024u);
+                        // B (K x N): MN-major, two 128-column halves B_STAGE/2
+                        //    apart (LBO), 8-row k groups 1024 B apart (SBO); the
+                        //    k-th slice of 32 rows starts 32*128 bytes in.
+                        // B (N x K): K-major like A.
+                        const uint64_t bdesc = B_KN ? smem_desc_sw128(b_addr + 4096u * kk, B_STAGE / 2, 1024u)
+                                                    : smem_desc_sw128(b_addr + 32u * kk, 16u, 1024u);
+                        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+                        if (INT8_KIND) mma_i8(d_tmem, adesc, bdesc, idesc, accum);
+                        else mma_f8f6f4(d_tmem, adesc, bdesc, idesc, accum);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+            }
+            // Every MMA issued by this thread completes before TMEM is freed.
+            tc_commit(done);
+            mbar_wait(done, 0, err);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+        const int row_in_tile = quarter * 32 + lane;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+            const int acc = it & 1;
+            const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
+            bool ok = mbar_wait(&tfull[acc], acc_phase, err);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int mb = tile % m_tiles, nb = tile / m_tiles;
+            const int row = mb * BM + row_in_tile;
+            const float rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + 32u * c, r);
+                tmem_ld_wait();
+                const int col0 = nb * BN + c * 32;
+                if (row < M && col0 < N) store_chunk<INT8_KIND>(ep, r, row, col0, N, rs);
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------- SIMT kernel (odd shapes) ----------------
+template <bool INT8_KIND>
+__global__ void __launch_bounds__(256) k_gemm_simt(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, int M,
+                                                   int N, int K, int b_kn, int fa, int fb, Epi ep) {
+    __shared__ float lut_a[256], lut_b[256];
+    if (!INT8_KIND) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+            lut_a[i] = fa == kE5M2 ? ocp_decode2<kE5M2>(i).x : ocp_decode2<kE4M3>(i).x;
+            lut_b[i] = fb == kE5M2 ? ocp_decode2<kE5M2>(i).x : ocp_decode2<kE4M3>(i).x;
+        }
+        __syncthreads();
+    }
+    const int col = blockIdx.x * 16 + (threadIdx.x & 15);
+    const int row = blockIdx.y * 16 + (threadIdx.x >> 4);
+    if (row >= M || col >= N) return;
+    const uint8_t* ar = a + static_cast<size_t>(row) * K;
+    uint32_t r[32];
+    if (INT8_KIND) {
+        int32_t s = 0;
+        for (int k = 0; k < K; ++k) {
+            const int32_t bv = static_cast<int8_t>(b_kn ? b[static_cast<size_t>(k) * N + col] : b[static_cast<size_t>(col) * K + k]);
+            s += static_cast<int32_t>(static_cast<int8_t>(ar[k])) * bv;
+        }
+        r[0] = static_cast<uint32_t>(s);
+    } else {
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const float bv = lut_b[b_kn ? b[static_cast<size_t>(k) * N + col] : b[static_cast<size_t>(col) * K + k]];
+            s = __fmaf_rn(lut_a[ar[k]], bv, s);
+        }
+        r[0] = __float_as_uint(s);
+    }
+    const float rs = ep.row_scale ? __ldg(ep.row_scale + row) : 1.0f;
+    if (INT8_KIND && ep.out_dtype == NQ_S32) {
+        static_cast<int32_t*>(ep.out)[static_cast<size_t>(row) * ep.ldo + col] = static_cast<int32_t>(r[0]);
+        return;
+    }
+    const float acc = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[0])) : __uint_as_float(r[0]);
+    const float v = epi_value(acc, ep.alpha, rs, ep.col_scale, ep.bias, col);
+    if (ep.out_dtype == NQ_BF16)
+        static_cast<uint16_t*>(ep.out)[static_cast<size_t>(row) * ep.ldo + col] = static_cast<uint16_t>(f32x2_to_bf16x2(v, 0.0f));
+    else
+        static_cast<float*>(ep.out)[static_cast<size_t>(row) * ep.ldo + col] = v;
+}
+
+// ---------------- host side ----------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+nq_status_t get_encode_fn(EncodeTiledFn* fn) {
+    static EncodeTiledFn cached = nullptr;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!cached) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+            return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+        cached = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    *fn = cached;
+    return NQ_SUCCESS;
+}
+
+// 2-D uint8 tensor map: inner extent `inner`, `outer` rows of `ld` bytes,
+// box {box_inner, box_outer}, 128-byte swizzle, zero fill out of bounds.
+nq_status_t make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                     uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn fn;
+    nq_status_t st = get_encode_fn(&fn);
+    if (st != NQ_SUCCESS) return st;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {ld};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return NQ_SUCCESS;
+}
+
+template <bool I8, bool KN>
+nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
+                      const DeviceInfo& di) {
+    CUtensorMap ma, mb;
+    nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, BM);
+    if (st != NQ_SUCCESS) return st;
+    if (KN) st = make_map(&mb, b, d.n, d.k, d.n, BN / 2, BK);
+    else st = make_map(&mb, b, d.k, d.n, d.k, BK, BN);
+    if (st != NQ_SUCCESS) return st;
+    uint32_t idesc;
+    if (I8) idesc = make_idesc(2u, 1u, 1u, KN ? 1u : 0u, BM, BN);
+    else idesc = make_idesc(1u, d.a_format == NQ_E5M2 ? 1u : 0u, d.b_format == NQ_E5M2 ? 1u : 0u, KN ? 1u : 0u, BM, BN);
+    auto kern = k_gemm_tc<I8, KN>;
+    // The shared-memory opt-in is a per-device function attribute.
+    static uint64_t attr_set = 0;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        const uint64_t bit = 1ull << (di.device & 63);
+        if (!(attr_set & bit)) {
+            NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+                          "cudaFuncSetAttribute(gemm)");
+            attr_set |= bit;
+        }
+    }
+    const int tiles = ((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
+    const int grid = std::max(1, std::min(tiles, di.sm_count));
+    uint32_t* err = device_error_word();
+    kern<<<grid, GEMM_THREADS, SMEM_BYTES, s>>>(ma, mb, d.m, d.n, d.k, idesc, ep, err);
+    NQ_LAUNCH_CHECK("nq_gemm (tcgen05)");
+    return NQ_SUCCESS;
+}
+
+}  // namespace
+
+nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, void* out, cudaStream_t s,
+                      int force_simt) {
+    if (!d) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: null descriptor");
+    if (d->m < 0 || d->n < 0 || d->k < 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: negative size");
+    if (d->m == 0 || d->n == 0) return NQ_SUCCESS;
+    if (!a || !b || !out) {
+        if (d->k > 0 || !out) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: null operand");
+    }
+    const bool i8 = d->a_format == NQ_INT8;
+    if (i8 != (d->b_format == NQ_INT8)) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: INT8 needs both operands INT8");
+    if (d->a_format < NQ_E4M3 || d->a_format > NQ_INT8 || d->b_format < NQ_E4M3 || d->b_format > NQ_INT8)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: format");
+    if (d->b_layout != NQ_B_KN && d->b_layout != NQ_B_NK) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: b_layout");
+    if (d->out_dtype != NQ_F32 && d->out_dtype != NQ_BF16 && !(i8 && d->out_dtype == NQ_S32))
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: out_dtype");
+    DeviceInfo di;
+    nq_status_t st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    Epi ep{out, d->n, d->out_dtype, d->alpha, d->row_scale, d->col_scale, d->bias};
+    const bool kn = d->b_layout == NQ_B_KN;
+    const bool tc_ok = !force_simt && d->k > 0 && d->k % 16 == 0 && d->n % 16 == 0 && aligned16(a) && aligned16(b) &&
+                       aligned16(out);
+    if (tc_ok) {
+        if (i8) return kn ? launch_tc<true, true>(*d, a, b, ep, s, di) : launch_tc<true, false>(*d, a, b, ep, s, di);
+        return kn ? launch_tc<false, true>(*d, a, b, ep, s, di) : launch_tc<false, false>(*d, a, b, ep, s, di);
+    }
+    dim3 grid((d->n + 15) / 16, (d->m + 15) / 16);
+    if (grid.y > 65535) return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm: M too large for the SIMT path");
+    const uint8_t* a8 = static_cast<const uint8_t*>(a);
+    const uint8_t* b8 = static_cast<const uint8_t*>(b);
+    if (i8) k_gemm_simt<true><<<grid, 256, 0, s>>>(a8, b8, d->m, d->n, d->k, kn, 0, 0, ep);
+    else k_gemm_simt<false><<<grid, 256, 0, s>>>(a8, b8, d->m, d->n, d->k, kn, d->a_format, d->b_format, ep);
+    NQ_LAUNCH_CHECK("nq_gemm (simt)");
+    return NQ_SUCCESS;
+}
+
+}  // namespace nq
+
+extern "C" {
+
+nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out, nq_stream_t s) {
+    return nq::gemm_impl(desc, a, b, out, s, 0);
+}
+
+// Test hook: the same GEMM forced onto the SIMT kernel (exact sequential-k).
+nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out, nq_stream_t s) {
+    return nq::gemm_impl(desc, a, b, out, s, 1);
+}
+
+static nq_status_t fp8_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k, int n, float sa, float sb,
+                               float so, nq_format_t f, nq_stream_t s) {
+    nq_gemm_desc_t d;
+    std::memset(&d, 0, sizeof(d));
+    d.m = m; d.n = n; d.k = k;
+    d.a_format = f; d.b_format = f;
+    d.b_layout = NQ_B_KN;
+    d.out_dtype = NQ_F32;
+    d.alpha = (sa * sb) * so;
+    return nq::gemm_impl(&d, a, b, out, s, 0);
+}
+
+nq_status_t nq_fp8_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k, int n, float scale_a,
+                                float scale_b, float scale_out, nq_stream_t s) {
+    return fp8_forward(a, b, out, m, k, n, scale_a, scale_b, scale_out, NQ_E4M3, s);
+}
+
+nq_status_t nq_fp8e5m2_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k, int n, float scale_a,
+                                    float scale_b, float scale_out, nq_stream_t s) {
+    return fp8_forward(a, b, out, m, k, n, scale_a, scale_b, scale_out, NQ_E5M2, s);
+}
+
+size_t nq_fp8_gemm_workspace_size(int m, int k, int n) {
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    return al(static_cast<size_t>(m) * k) + al(static_cast<size_t>(k) * n) + al(static_cast<size_t>(m) * n * sizeof(float));
+}
+
+}  // extern "C"

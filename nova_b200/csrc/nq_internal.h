@@ -1,0 +1,48 @@
+// Internal host-side helpers shared by the libnova_q translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/nova_q.h"
+
+namespace nq {
+
+// Records `msg` as this thread's last error and returns `st`.
+nq_status_t fail(nq_status_t st, const std::string& msg);
+// Maps a CUDA error to a status (with context) or NQ_SUCCESS.
+nq_status_t cuda_status(cudaError_t e, const char* what);
+
+struct DeviceInfo {
+    int device = -1;
+    int sm_count = 0;
+    int major = 0, minor = 0;
+    size_t max_smem_optin = 0;
+};
+// Properties of the current device (cached per device).
+nq_status_t current_device(DeviceInfo* out);
+
+// Stream-ordered scratch from a library-owned memory pool of the current
+// device: cudaMallocAsync after the first call on a device reuses the pool's
+// cached blocks instead of reaching the driver.
+nq_status_t scratch_alloc(void** p, size_t bytes, cudaStream_t s);
+void scratch_free(void* p, cudaStream_t s);
+
+// Device address of the error word of the current device (kernels OR their
+// error bits into it), or nullptr if it cannot be resolved.
+uint32_t* device_error_word();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace nq
+
+#define NQ_CHECK_CUDA(call, what)                                   \
+    do {                                                            \
+        cudaError_t e__ = (call);                                   \
+        if (e__ != cudaSuccess) return ::nq::cuda_status(e__, what); \
+    } while (0)
+
+#define NQ_LAUNCH_CHECK(what) NQ_CHECK_CUDA(cudaGetLastError(), what)

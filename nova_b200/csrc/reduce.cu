@@ -1,0 +1,529 @@
+// reduce.cu -- min/max, amax, histograms and per-row / per-column scaled
+// quantization (all HBM-bound).
+//
+// Whole-tensor reductions are single launches: every block reduces its
+// grid-stride share with 128-bit loads and warp shuffles, writes one partial to
+// stream-ordered scratch, and the last block to arrive (atomic ticket) folds the
+// partials and writes the result to device memory -- no host round trip, unlike
+// the reference's host-side finish (int8_kernels.cu:379-389).
+#include <algorithm>
+#include <cfloat>
+#include <cstring>
+#include <string>
+
+#include "codec.cuh"
+#include "nq_internal.h"
+
+namespace nq {
+
+nq_status_t quantize_scaled_impl(const void* src, nq_dtype_t dt, uint8_t* dst, size_t n, nq_format_t fmt,
+                                 const float* d_scale, cudaStream_t s);
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Block-wide min and max (all threads get the result).
+__device__ __forceinline__ float2 block_minmax(float lo, float hi) {
+    __shared__ float s_lo[32], s_hi[32];
+    lo = warp_min(lo);
+    hi = warp_max(hi);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { s_lo[w] = lo; s_hi[w] = hi; }
+    __syncthreads();
+    const int nw = blockDim.x >> 5;
+    lo = l < nw ? s_lo[l] : FLT_MAX;
+    hi = l < nw ? s_hi[l] : -FLT_MAX;
+    lo = warp_min(lo);
+    hi = warp_max(hi);
+    __syncthreads();
+    return make_float2(lo, hi);
+}
+
+template <class In>
+__device__ __forceinline__ void load4(const In* p, float (&x)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&x)[4]) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+template <>
+__device__ __forceinline__ void load4<uint16_t>(const uint16_t* p, float (&x)[4]) {
+    uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    x[0] = __uint_as_float(v.x << 16); x[1] = __uint_as_float(v.x & 0xFFFF0000u);
+    x[2] = __uint_as_float(v.y << 16); x[3] = __uint_as_float(v.y & 0xFFFF0000u);
+}
+__device__ __forceinline__ float ld1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ld1(const uint16_t* p) { return __uint_as_float(static_cast<uint32_t>(__ldg(p)) << 16); }
+
+// ABS = false: (min, max) of x.  ABS = true: (0-based) max of |x| in .y.
+// out: ABS=false -> out[0]=min, out[1]=max (or two separate pointers);
+//      ABS=true  -> out[0]=amax, out[1]=amax/qmax (1 if amax == 0).
+template <bool ABS, class In>
+__global__ void __launch_bounds__(kThreads) k_minmax(const In* __restrict__ src, size_t n, int vec,
+                                                     float* __restrict__ partials,
+                                                     unsigned int* __restrict__ ticket, float* out_lo,
+                                                     float* out_hi, float qmax) {
+    float lo = FLT_MAX, hi = ABS ? 0.0f : -FLT_MAX;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t n4 = vec ? n / 4 : 0;
+    // two independent 16-byte loads in flight per thread per step
+    size_t v = t0;
+    for (; v + stride < n4; v += 2 * stride) {
+        float x[4], y[4];
+        load4<In>(src + v * 4, x);
+        load4<In>(src + (v + stride) * 4, y);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (ABS) {
+                hi = fmaxf(hi, fmaxf(fabsf(x[i]), fabsf(y[i])));
+            } else {
+                lo = fminf(lo, fminf(x[i], y[i]));
+                hi = fmaxf(hi, fmaxf(x[i], y[i]));
+            }
+        }
+    }
+    for (; v < n4; v += stride) {
+        float x[4];
+        load4<In>(src + v * 4, x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (ABS) hi = fmaxf(hi, fabsf(x[i]));
+            else { lo = fminf(lo, x[i]); hi = fmaxf(hi, x[i]); }
+        }
+    }
+    for (size_t i = n4 * 4 + t0; i < n; i += stride) {
+        const float x = ld1(src + i);
+        if (ABS) hi = fmaxf(hi, fabsf(x));
+        else { lo = fminf(lo, x); hi = fmaxf(hi, x); }
+    }
+    float2 r = block_minmax(lo, hi);
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) {
+        partials[2 * blockIdx.x] = r.x;
+        partials[2 * blockIdx.x + 1] = r.y;
+        __threadfence();
+        const unsigned int t = atomicAdd(ticket, 1u);
+        s_last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    lo = FLT_MAX;
+    hi = ABS ? 0.0f : -FLT_MAX;
+    for (unsigned int b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+        lo = fminf(lo, __ldcg(partials + 2 * b));
+        hi = fmaxf(hi, __ldcg(partials + 2 * b + 1));
+    }
+    r = block_minmax(lo, hi);
+    if (threadIdx.x == 0) {
+        if (ABS) {
+            out_lo[0] = r.y;
+            out_lo[1] = r.y > 0.0f ? r.y / qmax : 1.0f;
+        } else {
+            *out_lo = r.x;
+            *out_hi = r.y;
+        }
+        *ticket = 0u;
+    }
+}
+
+// One block per row: min and max of the row (PerChannelCalibrator channels).
+__global__ void __launch_bounds__(kThreads) k_minmax_rows(const float* __restrict__ src, int cols,
+                                                          float* __restrict__ d_min, float* __restrict__ d_max) {
+    const float* row = src + static_cast<size_t>(blockIdx.x) * cols;
+    float lo = FLT_MAX, hi = -FLT_MAX;
+    const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15u) == 0);
+    const int n4 = vec ? cols / 4 : 0;
+    for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+        float x[4];
+        load4<float>(row + 4 * v, x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { lo = fminf(lo, x[i]); hi = fmaxf(hi, x[i]); }
+    }
+    for (int i = n4 * 4 + threadIdx.x; i < cols; i += blockDim.x) {
+        const float x = __ldg(row + i);
+        lo = fminf(lo, x);
+        hi = fmaxf(hi, x);
+    }
+    float2 r = block_minmax(lo, hi);
+    if (threadIdx.x == 0) {
+        d_min[blockIdx.x] = r.x;
+        d_max[blockIdx.x] = r.y;
+    }
+}
+
+// Histogram with a block-private shared copy of all bins (int8_kernels.cu:
+// 97-129 restated for any bin count): bin = (int)((x-min)/range*(bins-1)),
+// truncating and saturating like cvt.rzi, clamped to [0, bins-1].
+template <bool SHARED>
+__global__ void __launch_bounds__(kThreads) k_histogram(const float* __restrict__ src, size_t n, int vec,
+                                                        uint32_t* __restrict__ hist, float min_val, float range,
+                                                        int bins) {
+    extern __shared__ uint32_t s_hist[];
+    uint32_t* h = SHARED ? s_hist : hist;
+    if (SHARED) {
+        for (int i = threadIdx.x; i < bins; i += blockDim.x) s_hist[i] = 0;
+        __syncthreads();
+    }
+    const float mul = static_cast<float>(bins - 1);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t n4 = vec ? n / 4 : 0;
+    auto bin_of = [&](float x) {
+        int b = __float2int_rz((x - min_val) / range * mul);
+        return max(0, min(bins - 1, b));
+    };
+    for (size_t v = t0; v < n4; v += stride) {
+        float x[4];
+        load4<float>(src + 4 * v, x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) atomicAdd(h + bin_of(x[i]), 1u);
+    }
+    for (size_t i = n4 * 4 + t0; i < n; i += stride) atomicAdd(h + bin_of(__ldg(src + i)), 1u);
+    if (SHARED) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < bins; i += blockDim.x)
+            if (s_hist[i]) atomicAdd(hist + i, s_hist[i]);
+    }
+}
+
+// Per-row scaled quantize: scale = amax(row)/qmax (1 for a zero row),
+// q = encode(x / scale).  One block per row; the second pass re-reads the row
+// (from L1/L2: a row is at most a few tens of KB).
+template <int F, class In>
+__global__ void __launch_bounds__(kThreads) k_quant_rows(const In* __restrict__ src, uint8_t* __restrict__ dst,
+                                                         float* __restrict__ scales, int cols) {
+    const size_t r = blockIdx.x;
+    const In* row = src + r * static_cast<size_t>(cols);
+    uint8_t* out = dst + r * static_cast<size_t>(cols);
+    const bool vec = (cols % 16 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+    const int n4 = vec ? cols / 4 : 0;
+    float a = 0.0f;
+    for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+        float x[4];
+        load4<In>(row + 4 * v, x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a = fmaxf(a, fabsf(x[i]));
+    }
+    for (int i = n4 * 4 + threadIdx.x; i < cols; i += blockDim.x) a = fmaxf(a, fabsf(ld1(row + i)));
+    a = block_minmax(FLT_MAX, a).y;
+    const float s = a > 0.0f ? a / dev::FmtTraits<F>::qmax : 1.0f;
+    if (threadIdx.x == 0) scales[r] = s;
+    for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+        float x[4];
+        load4<In>(row + 4 * v, x);
+        const uint32_t p0 = dev::ocp_encode2<F>(x[0] / s, x[1] / s);
+        const uint32_t p1 = dev::ocp_encode2<F>(x[2] / s, x[3] / s);
+        reinterpret_cast<uint32_t*>(out)[v] = p0 | (p1 << 16);
+    }
+    for (int i = n4 * 4 + threadIdx.x; i < cols; i += blockDim.x)
+        out[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(ld1(row + i) / s, 0.0f) & 0xFFu);
+}
+
+// Per-column amax of a rows x cols matrix: grid.x over column groups of 4 x
+// 256, grid.y over row chunks; partial maxima of |x| (>= 0, so their float bit
+// patterns order like unsigned ints) are merged with atomicMax.
+__global__ void __launch_bounds__(kThreads) k_col_amax(const float* __restrict__ src, int rows, int cols,
+                                                       int rows_per_chunk, uint32_t* __restrict__ amax_bits) {
+    const int c4 = blockIdx.x * blockDim.x + threadIdx.x;  // group of 4 columns
+    const int c = c4 * 4;
+    if (c >= cols) return;
+    const int r0 = blockIdx.y * rows_per_chunk;
+    const int r1 = min(rows, r0 + rows_per_chunk);
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+    for (int r = r0; r < r1; ++r) {
+        const float* p = src + static_cast<size_t>(r) * cols + c;
+        if (vec) {
+            float x[4];
+            load4<float>(p, x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = fmaxf(a[i], fabsf(x[i]));
+        } else {
+            for (int i = 0; i < 4 && c + i < cols; ++i) a[i] = fmaxf(a[i], fabsf(__ldg(p + i)));
+        }
+    }
+    for (int i = 0; i < 4 && c + i < cols; ++i) atomicMax(amax_bits + c + i, __float_as_uint(a[i]));
+}
+
+template <int F>
+__global__ void __launch_bounds__(kThreads) k_quant_cols(const float* __restrict__ src, uint8_t* __restrict__ dst,
+                                                         const uint32_t* __restrict__ amax_bits,
+                                                         float* __restrict__ scales, int rows, int cols) {
+    const size_t total = static_cast<size_t>(rows) * cols;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = static_cast<int>(i % cols);
+        const float a = __uint_as_float(__ldg(amax_bits + c));
+        const float s = a > 0.0f ? a / dev::FmtTraits<F>::qmax : 1.0f;
+        if (i < static_cast<size_t>(cols)) scales[c] = s;
+        dst[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(__ldg(src + i) / s, 0.0f) & 0xFFu);
+    }
+}
+
+// ---- host helpers -----------------------------------------------------------------
+bool is_device_pointer(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+int reduce_grid(size_t n, int sm_count) {
+    const size_t want = (n / 4 + kThreads - 1) / kThreads;
+    return static_cast<int>(std::max<size_t>(1, std::min<size_t>(want, static_cast<size_t>(sm_count) * 4)));
+}
+
+// Launches the single-pass reduction with pool scratch.
+template <bool ABS, class In>
+nq_status_t launch_minmax(const In* src, size_t n, float* out_lo, float* out_hi, float qmax, cudaStream_t s,
+                          const char* what) {
+    DeviceInfo di;
+    nq_status_t st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    const int grid = reduce_grid(n, di.sm_count);
+    void* scratch = nullptr;
+    const size_t bytes = 256 + sizeof(float) * 2 * static_cast<size_t>(grid);
+    st = scratch_alloc(&scratch, bytes, s);
+    if (st != NQ_SUCCESS) return st;
+    unsigned int* ticket = static_cast<unsigned int*>(scratch);
+    float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + 256);
+    cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(unsigned int), s);
+    if (e == cudaSuccess) {
+        const int vec = aligned16(src);
+        k_minmax<ABS, In><<<grid, kThreads, 0, s>>>(src, n, vec, partials, ticket, out_lo, out_hi, qmax);
+        e = cudaGetLastError();
+    }
+    scratch_free(scratch, s);
+    return cuda_status(e, what);
+}
+
+float qmax_of(nq_format_t f) { return f == NQ_E4M3 ? 448.0f : (f == NQ_E5M2 ? 57344.0f : 127.0f); }
+
+}  // namespace
+
+nq_status_t amax_scale_impl(const void* data, nq_dtype_t dt, size_t n, nq_format_t fmt, float* d_out,
+                            cudaStream_t s) {
+    if (!d_out || (n && !data)) return fail(NQ_ERROR_INVALID_VALUE, "nq_amax_scale_async: null pointer");
+    if (fmt != NQ_E4M3 && fmt != NQ_E5M2 && fmt != NQ_INT8)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_amax_scale_async: format");
+    if (n == 0) {
+        const float v[2] = {0.0f, 1.0f};
+        return cuda_status(cudaMemcpyAsync(d_out, v, sizeof(v), cudaMemcpyHostToDevice, s), "nq_amax_scale_async");
+    }
+    if (dt == NQ_F32)
+        return launch_minmax<true, float>(static_cast<const float*>(data), n, d_out, nullptr, qmax_of(fmt), s,
+                                          "nq_amax_scale_async");
+    if (dt == NQ_BF16)
+        return launch_minmax<true, uint16_t>(static_cast<const uint16_t*>(data), n, d_out, nullptr, qmax_of(fmt),
+                                             s, "nq_amax_scale_async");
+    return fail(NQ_ERROR_INVALID_VALUE, "nq_amax_scale_async: src dtype");
+}
+
+}  // namespace nq
+
+using nq::fail;
+
+extern "C" {
+
+nq_status_t nq_minmax_async(const float* data, size_t n, float* d_out, nq_stream_t s) {
+    if (!d_out || (n && !data)) return fail(NQ_ERROR_INVALID_VALUE, "nq_minmax_async: null pointer");
+    if (n == 0) return nq::cuda_status(cudaMemsetAsync(d_out, 0, 2 * sizeof(float), s), "nq_minmax_async");
+    return nq::launch_minmax<false, float>(data, n, d_out, d_out + 1, 0.0f, s, "nq_minmax_async");
+}
+
+nq_status_t nq_compute_minmax(const float* data, size_t n, float* min_val, float* max_val, nq_stream_t s) {
+    if (!min_val || !max_val) return fail(NQ_ERROR_INVALID_VALUE, "nq_compute_minmax: null output");
+    const bool out_dev = nq::is_device_pointer(min_val) && nq::is_device_pointer(max_val);
+    if (n == 0) {  // int8_kernels.cu:331-335
+        if (out_dev) {
+            NQ_CHECK_CUDA(cudaMemsetAsync(min_val, 0, sizeof(float), s), "nq_compute_minmax");
+            NQ_CHECK_CUDA(cudaMemsetAsync(max_val, 0, sizeof(float), s), "nq_compute_minmax");
+            NQ_CHECK_CUDA(cudaStreamSynchronize(s), "nq_compute_minmax");
+        } else {
+            *min_val = 0.0f;
+            *max_val = 0.0f;
+        }
+        return NQ_SUCCESS;
+    }
+    if (!data) return fail(NQ_ERROR_INVALID_VALUE, "nq_compute_minmax: null data");
+    // Host input: stage it through pooled device memory (int8_kernels.cu:337-357).
+    const float* d_data = data;
+    void* staged = nullptr;
+    void* res = nullptr;
+    nq_status_t st = NQ_SUCCESS;
+    if (!nq::is_device_pointer(data)) {
+        st = nq::scratch_alloc(&staged, n * sizeof(float), s);
+        if (st != NQ_SUCCESS) return st;
+        cudaError_t e = cudaMemcpyAsync(staged, data, n * sizeof(float), cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) { nq::scratch_free(staged, s); return nq::cuda_status(e, "nq_compute_minmax: H2D"); }
+        d_data = static_cast<const float*>(staged);
+    }
+    float* lo = min_val;
+    float* hi = max_val;
+    if (!out_dev) {
+        st = nq::scratch_alloc(&res, 2 * sizeof(float), s);
+        if (st != NQ_SUCCESS) { nq::scratch_free(staged, s); return st; }
+        lo = static_cast<float*>(res);
+        hi = lo + 1;
+    }
+    st = nq::launch_minmax<false, float>(d_data, n, lo, hi, 0.0f, s, "nq_compute_minmax");
+    float h[2] = {0.0f, 0.0f};
+    if (st == NQ_SUCCESS && !out_dev)
+        st = nq::cuda_status(cudaMemcpyAsync(h, res, sizeof(h), cudaMemcpyDeviceToHost, s), "nq_compute_minmax: D2H");
+    nq::scratch_free(staged, s);
+    nq::scratch_free(res, s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (st != NQ_SUCCESS) return st;
+    if (e != cudaSuccess) return nq::cuda_status(e, "nq_compute_minmax: synchronize");
+    if (!out_dev) {
+        *min_val = h[0];
+        *max_val = h[1];
+    }
+    return NQ_SUCCESS;
+}
+
+nq_status_t nq_build_histogram(const float* data, uint32_t* histogram, size_t n, float min_val, float max_val,
+                               int num_bins, nq_stream_t s) {
+    if (!histogram || num_bins < 1 || num_bins > 65536)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_build_histogram: bad histogram or num_bins");
+    if (n && !data) return fail(NQ_ERROR_INVALID_VALUE, "nq_build_histogram: null data");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    NQ_CHECK_CUDA(cudaMemsetAsync(histogram, 0, sizeof(uint32_t) * num_bins, s), "nq_build_histogram: memset");
+    const float range = max_val - min_val;
+    if (n == 0 || !(range > 1e-6f)) {
+        NQ_CHECK_CUDA(cudaStreamSynchronize(s), "nq_build_histogram");
+        return NQ_SUCCESS;
+    }
+    const float* d_data = data;
+    void* staged = nullptr;
+    if (!nq::is_device_pointer(data)) {
+        st = nq::scratch_alloc(&staged, n * sizeof(float), s);
+        if (st != NQ_SUCCESS) return st;
+        cudaError_t e = cudaMemcpyAsync(staged, data, n * sizeof(float), cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) { nq::scratch_free(staged, s); return nq::cuda_status(e, "nq_build_histogram: H2D"); }
+        d_data = static_cast<const float*>(staged);
+    }
+    const int grid = nq::reduce_grid(n, di.sm_count);
+    const int vec = nq::aligned16(d_data);
+    const size_t smem = sizeof(uint32_t) * static_cast<size_t>(num_bins);
+    cudaError_t e;
+    if (smem <= 48 * 1024) {
+        nq::k_histogram<true><<<grid, nq::kThreads, smem, s>>>(d_data, n, vec, histogram, min_val, range, num_bins);
+    } else if (smem <= 200 * 1024) {
+        cudaFuncSetAttribute(nq::k_histogram<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        nq::k_histogram<true><<<grid, nq::kThreads, smem, s>>>(d_data, n, vec, histogram, min_val, range, num_bins);
+    } else {
+        nq::k_histogram<false><<<grid, nq::kThreads, 0, s>>>(d_data, n, vec, histogram, min_val, range, num_bins);
+    }
+    e = cudaGetLastError();
+    nq::scratch_free(staged, s);
+    cudaError_t e2 = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return nq::cuda_status(e, "nq_build_histogram: launch");
+    return nq::cuda_status(e2, "nq_build_histogram: synchronize");
+}
+
+nq_status_t nq_amax_scale_async(const void* data, nq_dtype_t src_dtype, size_t n, nq_format_t fmt, float* d_out,
+                                nq_stream_t s) {
+    return nq::amax_scale_impl(data, src_dtype, n, fmt, d_out, s);
+}
+
+nq_status_t nq_minmax_rows(const float* data, int rows, int cols, float* d_min, float* d_max, nq_stream_t s) {
+    if (rows < 0 || cols < 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_minmax_rows: negative size");
+    if (rows == 0) return NQ_SUCCESS;
+    if (!data || !d_min || !d_max) return fail(NQ_ERROR_INVALID_VALUE, "nq_minmax_rows: null pointer");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    nq::k_minmax_rows<<<rows, nq::kThreads, 0, s>>>(data, cols, d_min, d_max);
+    NQ_LAUNCH_CHECK("nq_minmax_rows");
+    return NQ_SUCCESS;
+}
+
+nq_status_t nq_calibrate_quantize(const void* src, nq_dtype_t src_dtype, uint8_t* dst, size_t n, nq_format_t fmt,
+                                  float* d_amax_scale, nq_stream_t s) {
+    nq_status_t st = nq::amax_scale_impl(src, src_dtype, n, fmt, d_amax_scale, s);
+    if (st != NQ_SUCCESS) return st;
+    return nq::quantize_scaled_impl(src, src_dtype, dst, n, fmt, d_amax_scale + 1, s);
+}
+
+nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst, float* scales, int rows,
+                             int cols, nq_format_t fmt, nq_stream_t s) {
+    if (rows < 0 || cols < 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: negative size");
+    if (rows == 0 || cols == 0) return NQ_SUCCESS;
+    if (!src || !dst || !scales) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: null pointer");
+    if (src_dtype != NQ_F32 && src_dtype != NQ_BF16) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: dtype");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    using namespace nq::dev;
+#define NQ_QROWS(F)                                                                                       \
+    (src_dtype == NQ_F32                                                                                  \
+         ? nq::k_quant_rows<F, float><<<rows, nq::kThreads, 0, s>>>(static_cast<const float*>(src), dst,  \
+                                                                    scales, cols)                         \
+         : nq::k_quant_rows<F, uint16_t><<<rows, nq::kThreads, 0, s>>>(static_cast<const uint16_t*>(src), \
+                                                                       dst, scales, cols))
+    switch (fmt) {
+        case NQ_E4M3: NQ_QROWS(kE4M3); break;
+        case NQ_E5M2: NQ_QROWS(kE5M2); break;
+        case NQ_INT8: NQ_QROWS(kINT8); break;
+        default: return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: format");
+    }
+#undef NQ_QROWS
+    NQ_LAUNCH_CHECK("nq_quantize_rows");
+    return NQ_SUCCESS;
+}
+
+nq_status_t nq_quantize_cols(const float* src, uint8_t* dst, float* scales, int rows, int cols, nq_format_t fmt,
+                             nq_stream_t s) {
+    if (rows < 0 || cols < 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_cols: negative size");
+    if (rows == 0 || cols == 0) return NQ_SUCCESS;
+    if (!src || !dst || !scales) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_cols: null pointer");
+    if (fmt != NQ_E4M3 && fmt != NQ_E5M2 && fmt != NQ_INT8)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_cols: format");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    void* amax = nullptr;
+    st = nq::scratch_alloc(&amax, sizeof(uint32_t) * static_cast<size_t>(cols), s);
+    if (st != NQ_SUCCESS) return st;
+    cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(uint32_t) * static_cast<size_t>(cols), s);
+    if (e == cudaSuccess) {
+        const int groups = (cols + 4 * nq::kThreads - 1) / (4 * nq::kThreads);
+        const int chunks = std::max(1, std::min(rows, (di.sm_count * 8 + groups - 1) / groups));
+        const int rpc = (rows + chunks - 1) / chunks;
+        dim3 g1(groups, (rows + rpc - 1) / rpc);
+        nq::k_col_amax<<<g1, nq::kThreads, 0, s>>>(src, rows, cols, rpc, static_cast<uint32_t*>(amax));
+        const size_t total = static_cast<size_t>(rows) * cols;
+        const int g2 = static_cast<int>(std::min<size_t>((total + nq::kThreads - 1) / nq::kThreads,
+                                                         static_cast<size_t>(di.sm_count) * 8));
+        const uint32_t* ab = static_cast<const uint32_t*>(amax);
+        switch (fmt) {
+            case NQ_E4M3: nq::k_quant_cols<nq::dev::kE4M3><<<g2, nq::kThreads, 0, s>>>(src, dst, ab, scales, rows, cols); break;
+            case NQ_E5M2: nq::k_quant_cols<nq::dev::kE5M2><<<g2, nq::kThreads, 0, s>>>(src, dst, ab, scales, rows, cols); break;
+            default: nq::k_quant_cols<nq::dev::kINT8><<<g2, nq::kThreads, 0, s>>>(src, dst, ab, scales, rows, cols); break;
+        }
+        e = cudaGetLastError();
+    }
+    nq::scratch_free(amax, s);
+    return nq::cuda_status(e, "nq_quantize_cols");
+}
+
+}  // extern "C"

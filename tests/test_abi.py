@@ -1,0 +1,72 @@
+"""The C ABI library loads and exports every entry point include/*.h declares
+(CPU only: no kernel is launched)."""
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for d, _, files in os.walk(inc):
+        for f in files:
+            if f.endswith(".h"):
+                txt = open(os.path.join(d, f)).read()
+                txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+                names |= set(re.findall(r"\b(nq_[a-z0-9_]+)\s*\(", txt))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    import nova_b200.capi as capi
+    out = subprocess.run(["nm", "-D", "--defined-only", capi.LIB_PATH if hasattr(capi, "LIB_PATH") else
+                          os.path.join(ROOT, "nova_b200", "libnova_q.so")], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (nq_\w+)", out))
+    declared = declared_symbols()
+    assert declared, "no declarations found"
+    assert declared <= exported, f"declared but not exported: {sorted(declared - exported)}"
+    assert exported <= declared, f"exported but not declared: {sorted(exported - declared)}"
+    for name in declared:
+        assert hasattr(capi.lib, name)
+
+
+def test_status_strings_and_errors_without_gpu():
+    import ctypes as C
+    import nova_b200.capi as capi
+    assert capi.lib.nq_status_string(0) == b"NQ_SUCCESS"
+    assert capi.lib.nq_status_string(6) == b"NQ_ERROR_DEVICE_TIMEOUT"
+    assert capi.lib.nq_version() >= 100
+    # argument errors are reported before any device work
+    st = capi.quantize_f32_to_int8.raw(None, None, 10, 1.0, 0.0, 1, None)
+    assert st == 1 and b"null" in capi.lib.nq_last_error()
+    assert capi.quantize_f32_to_int8.raw(None, None, 0, 1.0, 0.0, 1, None) == 0
+    d = capi.make_desc(16, 16, 16, capi.E4M3, capi.INT8)
+    assert capi.gemm.raw(C.byref(d), 16, 16, 16, None) == 1
+    assert capi.lib.nq_fp8_gemm_workspace_size(128, 256, 128) == 128 * 256 + 256 * 128 + 128 * 128 * 4
+
+
+def test_no_device_is_an_error_not_a_crash():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    import nova_b200.capi as capi
+    st = capi.quantize_f32_to_int8.raw(16, 32, 10, 1.0, 0.0, 1, None)
+    assert st in (3, 5)
+
+
+def test_cpp_headers_compile():
+    """The drop-in C++ headers compile on their own (syntax check)."""
+    inc = os.path.join(ROOT, "include")
+    hdrs = []
+    for d, _, files in os.walk(os.path.join(inc, "cuda")):
+        hdrs += [os.path.join(d, f) for f in files if f.endswith(".hpp")]
+    if not hdrs:
+        pytest.skip("no C++ headers")
+    src = "".join(f'#include "{h}"\n' for h in sorted(hdrs)) + "int main(){return 0;}\n"
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", inc, "-I", "/usr/local/cuda/include", "-x", "c++", "-"],
+                       input=src, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

@@ -1,0 +1,180 @@
+"""tcgen05 GEMMs against the CPU oracle.
+
+INT8 (kind::i8): the int32 accumulators must be exact and the scaled
+fp32/bf16 outputs bit-identical to the oracle's epilogue (same operation
+order, one rounding per step).
+FP8 (kind::f8f6f4): products of two FP8 values are exact in fp32, only the
+summation order differs from the oracle's sequential FMA; the bar is a max
+relative error of 1e-2 per element (with |ref| floored at 1e-2 * rms(ref)),
+and in practice the observed error is far smaller (asserted separately for
+fp32 outputs at 1e-4)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+FP8_TOL = 1e-2
+FP8_TOL_F32_OBSERVED = 1e-4
+
+
+@pytest.fixture(scope="module")
+def nq(cuda):
+    import nova_b200.capi as capi
+    return capi
+
+
+def fp8_operand(shape, seed, fmt):
+    import oracle_lib as O
+    x = np.random.default_rng(seed).standard_normal(shape).astype(np.float32)
+    qmax = 448.0 if fmt == 0 else 57344.0
+    s = float(np.abs(x).max() / qmax)
+    return O.quantize_ocp(x, s, fmt), s
+
+
+def int8_operand(shape, seed):
+    return np.random.default_rng(seed).integers(-127, 128, size=shape, dtype=np.int8)
+
+
+def rel_err(got, ref):
+    got = got.astype(np.float64)
+    ref = ref.astype(np.float64)
+    floor = 1e-2 * np.sqrt(np.mean(ref * ref)) + 1e-30
+    return float(np.max(np.abs(got - ref) / np.maximum(np.abs(ref), floor)))
+
+
+def run_gemm(nq, a, b, m, n, k, fa, fb, b_layout, out_dtype, alpha=1.0, row=None, col=None, bias=None,
+             simt=False):
+    from gpu_util import dev, empty, host, ptr, stream
+    d_a, d_b = dev(a), dev(b)
+    esize = 2 if out_dtype == 1 else 4
+    d_o = empty(m * n * esize)
+    d_r = dev(row) if row is not None else None
+    d_c = dev(col) if col is not None else None
+    d_bi = dev(bias) if bias is not None else None
+    desc = nq.make_desc(m, n, k, fa, fb, b_layout, out_dtype, alpha, ptr(d_r) if d_r is not None else 0,
+                        ptr(d_c) if d_c is not None else 0, ptr(d_bi) if d_bi is not None else 0)
+    (nq.gemm_simt if simt else nq.gemm)(desc, ptr(d_a), ptr(d_b), ptr(d_o), stream())
+    dt = {0: np.float32, 1: np.uint16, 2: np.int32}[out_dtype]
+    out = host(d_o, dt, (m, n))
+    assert nq.device_error_flags() == 0
+    return out
+
+
+SHAPES = [(128, 256, 128), (256, 512, 256), (200, 272, 176), (128, 1024, 1024), (384, 768, 4096), (64, 16, 32)]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("b_layout", [0, 1])
+def test_int8_gemm_exact(nq, m, n, k, b_layout):
+    import oracle_lib as O
+    a = int8_operand((m, k), m + k)
+    b = int8_operand((k, n) if b_layout == 0 else (n, k), n + k + 1)
+    acc = run_gemm(nq, a, b, m, n, k, 2, 2, b_layout, 2)
+    np.testing.assert_array_equal(acc, O.gemm_i8_acc(a, b, b_layout == 0))
+    rs = (np.random.default_rng(1).random(m) * 0.01 + 1e-3).astype(np.float32)
+    cs = (np.random.default_rng(2).random(n) * 0.01 + 1e-3).astype(np.float32)
+    bias = np.random.default_rng(3).standard_normal(n).astype(np.float32)
+    for out_dtype in (0, 1):
+        got = run_gemm(nq, a, b, m, n, k, 2, 2, b_layout, out_dtype, 0.75, rs, cs, bias)
+        np.testing.assert_array_equal(got, O.epilogue(acc, out_dtype == 1, 0.75, rs, cs, bias))
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("b_layout", [0, 1])
+@pytest.mark.parametrize("fa,fb", [(0, 0), (1, 1), (0, 1)])
+def test_fp8_gemm_vs_oracle(nq, m, n, k, b_layout, fa, fb):
+    import oracle_lib as O
+    a, sa = fp8_operand((m, k), 10 + m, fa)
+    b, sb = fp8_operand((k, n) if b_layout == 0 else (n, k), 20 + n, fb)
+    ref_acc = O.gemm_fp8_acc(a, b, fa, fb, b_layout == 0)
+    alpha = np.float32(sa) * np.float32(sb)
+    got32 = run_gemm(nq, a, b, m, n, k, fa, fb, b_layout, 0, float(alpha))
+    ref32 = O.epilogue(ref_acc, False, float(alpha))
+    assert rel_err(got32, ref32) <= FP8_TOL_F32_OBSERVED
+    got16 = run_gemm(nq, a, b, m, n, k, fa, fb, b_layout, 1, float(alpha))
+    ref16 = O.epilogue(ref_acc, True, float(alpha))
+    assert rel_err(O.bf16_bits_to_f32(got16), O.bf16_bits_to_f32(ref16)) <= FP8_TOL
+
+
+def test_fp8_gemm_scales_bias_bf16(nq):
+    import oracle_lib as O
+    m, n, k = 256, 512, 384
+    a, _ = fp8_operand((m, k), 1, 0)
+    b, _ = fp8_operand((n, k), 2, 0)
+    rs = (np.random.default_rng(5).random(m) + 0.5).astype(np.float32)
+    cs = (np.random.default_rng(6).random(n) + 0.5).astype(np.float32)
+    bias = np.random.default_rng(7).standard_normal(n).astype(np.float32)
+    got = run_gemm(nq, a, b, m, n, k, 0, 0, 1, 1, 0.001, rs, cs, bias)
+    ref = O.epilogue(O.gemm_fp8_acc(a, b, 0, 0, False), True, 0.001, rs, cs, bias)
+    assert rel_err(O.bf16_bits_to_f32(got), O.bf16_bits_to_f32(ref)) <= FP8_TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(4, 4, 4), (33, 17, 9), (100, 40, 30), (16, 24, 1000)])
+def test_simt_path_exact(nq, m, n, k):
+    """Shapes the TMA path cannot take run the SIMT kernel: sequential-k FMA,
+    bit-identical to the oracle."""
+    import oracle_lib as O
+    a, _ = fp8_operand((m, k), m, 0)
+    b, _ = fp8_operand((k, n), n, 0)
+    got = run_gemm(nq, a, b, m, n, k, 0, 0, 0, 0, 1.0)
+    np.testing.assert_array_equal(got, O.epilogue(O.gemm_fp8_acc(a, b, 0, 0, True), False, 1.0))
+    ai, bi = int8_operand((m, k), 1), int8_operand((k, n), 2)
+    np.testing.assert_array_equal(run_gemm(nq, ai, bi, m, n, k, 2, 2, 0, 2), O.gemm_i8_acc(ai, bi, True))
+
+
+def test_reference_fp8_gemm_cases(nq):
+    """fp8_gemm_test.cpp: 4x4 times identity (:58-108), 8x8 identity
+    (:110-162), config scaling (:210-275) through FP8GEMM::forward's entry
+    point, codes made by the reference codec FP8E4M3(float)."""
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    eye4 = np.eye(4, dtype=np.float32)
+    a = np.arange(1, 17, dtype=np.float32).reshape(4, 4)
+    for (x, y, sa, sb, expect) in [(a, eye4, 1.0, 1.0, a), (np.eye(8, dtype=np.float32), np.eye(8, dtype=np.float32),
+                                                            1.0, 1.0, np.eye(8, dtype=np.float32)),
+                                   (np.tile(np.arange(1, 5, dtype=np.float32), (4, 1)), eye4, 2.0, 0.5,
+                                    np.tile(np.arange(1, 5, dtype=np.float32), (4, 1)))]:
+        m, k = x.shape
+        n = y.shape[1]
+        qa, qb = O.quantize_compat(x), O.quantize_compat(y)
+        d_a, d_b, d_c = dev(qa), dev(qb), empty(4 * m * n)
+        nq.fp8_gemm_forward(ptr(d_a), ptr(d_b), ptr(d_c), m, k, n, sa, sb, 1.0, stream())
+        c = host(d_c, np.float32, (m, n))
+        np.testing.assert_allclose(c, expect, rtol=0.05, atol=1e-6)
+    assert nq.lib.nq_fp8_gemm_workspace_size(128, 256, 128) >= max(128 * 256, 256 * 128, 128 * 128 * 4)
+
+
+def test_c1_shape_fp8_forward(nq):
+    """FP8GEMM::forward M=128, K=1024, N=1024, fp32 out."""
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    m, k, n = 128, 1024, 1024
+    a, sa = fp8_operand((m, k), 1, 0)
+    b, sb = fp8_operand((k, n), 0, 0)
+    d_a, d_b, d_c = dev(a), dev(b), empty(4 * m * n)
+    nq.fp8_gemm_forward(ptr(d_a), ptr(d_b), ptr(d_c), m, k, n, sa, sb, 1.0, stream())
+    got = host(d_c, np.float32, (m, n))
+    ref = O.epilogue(O.gemm_fp8_acc(a, b, 0, 0, True), False, float(np.float32(sa) * np.float32(sb)))
+    assert rel_err(got, ref) <= FP8_TOL_F32_OBSERVED
+
+
+def test_large_fp8_gemm_torch_check(nq):
+    """4096^3 checked against a torch fp64 matmul of
+    the decoded operands: too large for the C oracle in a test."""
+    import torch
+    from gpu_util import ptr, stream
+    m = n = k = 4096
+    g = torch.Generator(device="cuda").manual_seed(2)
+    A = torch.randn(m, k, device="cuda", generator=g)
+    B = torch.randn(k, n, device="cuda", generator=g)
+    sa, sb = float(A.abs().max() / 448), float(B.abs().max() / 448)
+    qa = (A / sa).to(torch.float8_e4m3fn)
+    qb = (B / sb).to(torch.float8_e4m3fn)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    desc = nq.make_desc(m, n, k, 0, 0, 0, 1, float(np.float32(sa) * np.float32(sb)))
+    nq.gemm(desc, qa.data_ptr(), qb.data_ptr(), out.data_ptr(), stream())
+    ref = (qa.double() @ qb.double()) * (float(np.float32(sa) * np.float32(sb)))
+    ref_bf = ref.to(torch.bfloat16).double()
+    err = ((out.double() - ref_bf).abs() / torch.maximum(ref_bf.abs(), 1e-2 * ref_bf.pow(2).mean().sqrt())).max()
+    assert float(err) <= FP8_TOL
+    assert nq.device_error_flags() == 0
