@@ -1,0 +1,362 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized-inference hot path (pplmx/nova cuda::quantize on B200).
+
+Headline workload: dense FP8 E4M3 GEMM, M=N=K=4096,
+A and B pre-quantized from fp32 ~N(0,1) with per-tensor scales amax/448, fp32
+accumulation, bf16 output with the scales folded into the epilogue; B in the
+reference's K x N layout (FP8GEMM::forward).  One step = one GEMM launch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun): every rank runs the same GEMM on its own GPU (replicas, no
+collective on the data path); value = all ranks' FLOPs / max-over-ranks time.
+--impl reference times the reference algorithm on the host cores (the CPU
+oracle port of FP8GEMM::forward's naive kernel, fp8_gemm.cu:64-86), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = N = K = 4096
+FLOPS = 2.0 * M * N * K
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+METRIC = "FP8 GEMM TFLOPS (4096^3 E4M3, bf16 out)"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch from the committed ncu summary, or None."""
+    try:
+        txt = open(os.path.join(ROOT, "profiles", name)).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, index, period=0.002):
+        self.index, self.period = index, period
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+            return self
+        names = {
+            "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+            "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4, "sync_boost": 0x10,
+        }
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                    r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    for k, bit in names.items():
+                        if r & bit:
+                            self.reasons.add(k)
+                except Exception:
+                    pass
+                time.sleep(self.period)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples),
+                "source": "nvml"}
+
+
+def dist_init(gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_operands(seed_a=2, seed_b=3):
+    """A, B ~ N(0,1) quantized on the GPU with per-tensor amax/448 scales
+    (nq_calibrate_quantize: amax -> scale -> OCP E4M3 codes)."""
+    import torch
+    import nova_b200.capi as nq
+    s = torch.cuda.current_stream().cuda_stream
+    out = []
+    for seed in (seed_a, seed_b):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        x = torch.randn(M, K, device="cuda", generator=g)
+        q = torch.empty(M * K, dtype=torch.uint8, device="cuda")
+        sc = torch.empty(2, dtype=torch.float32, device="cuda")
+        nq.calibrate_quantize(x.data_ptr(), nq.F32, q.data_ptr(), x.numel(), nq.E4M3, sc.data_ptr(), s)
+        torch.cuda.synchronize()
+        out.append((q, float(sc[1].item())))
+        del x
+    return out
+
+
+def cpu_reference_sample(rows, threads):
+    """Times the oracle port of the reference FP8 GEMM (naive kernel order,
+    compat decode, fp32 FMA) on `rows` rows of the 4096^3 problem."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    rng = np.random.default_rng(0)
+    a = rng.integers(0, 256, (rows, K), dtype=np.uint8)
+    b = rng.integers(0, 256, (K, N), dtype=np.uint8)
+    c = np.empty((rows, N), np.float32)
+    t0 = time.perf_counter()
+    used = O.lib.orc_fp8_gemm_reference_rows_mt(O.ptr(a), O.ptr(b), O.ptr(c), rows, K, N, 1.0, 1.0, 1.0, 0, rows,
+                                                threads)
+    dt = time.perf_counter() - t0
+    return dt, used
+
+
+def cpu_baseline(target_s=8.0):
+    threads = os.cpu_count() or 1
+    dt, used = cpu_reference_sample(max(1, threads), threads)     # calibration
+    rate = (2.0 * max(1, threads) * N * K) / dt
+    rows = int(max(threads, min(M, target_s * rate / (2.0 * N * K))))
+    dt, used = cpu_reference_sample(rows, threads)
+    tflops = 2.0 * rows * N * K / dt / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": used, "kind": "port",
+            "sample": f"{rows} of 4096 rows of the 4096^3 FP8 GEMM (naive reference order), {dt:.1f} s"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    rows = max(threads, 8)
+    for _ in range(args.warmup):
+        cpu_reference_sample(rows, threads)
+    times = []
+    used = threads
+    for _ in range(args.steps):
+        dt, used = cpu_reference_sample(rows, threads)
+        times.append(dt)
+    per_step = sum(times) / len(times)
+    tflops = 2.0 * rows * N * K / per_step / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "fp8_gemm_4096 (BASELINE configs[1]), host sample", "m": M, "n": N, "k": K,
+                   "rows_per_step": rows},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": used, "kind": "port",
+                         "sample": f"{rows} of 4096 rows per step (oracle port of fp8_gemm.cu:64-86)"},
+        "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = dist_init(args.gpus)
+    import nova_b200.capi as nq
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    (qa, sa), (qb, sb) = make_operands()
+    alpha = float(__import__("numpy").float32(sa) * __import__("numpy").float32(sb))
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    desc = nq.make_desc(M, N, K, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, alpha)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def gemm():
+        nq.gemm(desc, qa.data_ptr(), qb.data_ptr(), out.data_ptr(), sh)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        gemm()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        r0.record(stream)
+        for i in range(args.steps):
+            flush.zero_()                     # L2 flush between timed launches
+            starts[i].record(stream)
+            gemm()
+            ends[i].record(stream)
+        r1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    mean_ms = sum(launch_ms) / len(launch_ms)
+    region_ms = r0.elapsed_time(r1)
+    mean_ms_max = max_over_ranks(mean_ms, world)
+    value = world * FLOPS / (mean_ms_max * 1e-3) / 1e12
+    assert nq.device_error_flags() == 0, "a kernel reported a timed-out wait"
+
+    # ---- end to end through the C ABI with host buffers -------------------
+    ha = torch.empty(M * K, dtype=torch.uint8, pin_memory=True)
+    hb = torch.empty(K * N, dtype=torch.uint8, pin_memory=True)
+    hc = torch.empty(M, N, dtype=torch.bfloat16, pin_memory=True)
+    ha.copy_(qa.cpu())
+    hb.copy_(qb.cpu())
+    da = torch.empty_like(qa)
+    db = torch.empty_like(qb)
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step():
+        da.copy_(ha, non_blocking=True)
+        db.copy_(hb, non_blocking=True)
+        nq.gemm(desc, da.data_ptr(), db.data_ptr(), out.data_ptr(), sh)
+        hc.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    e2e_value = world * FLOPS / (e2e_ms * 1e-3) / 1e12
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return 0
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    achieved = FLOPS / (mean_ms * 1e-3) / 1e12
+    traffic = profile_traffic("fp8_gemm_4096.md")
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_ms_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 in, fp32 accumulate, bf16 out", "data": "synthetic",
+        "config": {"workload": "fp8_gemm_4096 (BASELINE configs[1])", "m": M, "n": N, "k": K,
+                   "b_layout": "K x N row-major (FP8GEMM::forward)", "parallelism": f"replicas x{world}",
+                   "l2": "256 MiB buffer written between timed launches", "timed_region_ms": region_ms},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": achieved / fp8_peak, "traffic": traffic,
+                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({pk['source']}): dense FP8 = 2x dense bf16 on B200"},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * M * K,
+                "d2h_bytes_per_step": 2 * M * N, "path": "nq_gemm C ABI, pinned host A/B in, bf16 C out"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if args.cublas:
+        line["library_comparison"] = cublaslt_fp8(args.steps, args.warmup, flush)
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cublaslt_fp8(steps, warmup, flush):
+    """cuBLASLt FP8 (torch._scaled_mm, e4m3 x e4m3 -> bf16, per-tensor scales)
+    on the same shape, timed the same way: the library number to beat, and at
+    8192^3 the practical dense FP8 ceiling of the part."""
+    import torch
+    res = {}
+    for size in (4096, 8192):
+        a = torch.randn(size, size, device="cuda").to(torch.float8_e4m3fn)
+        b = torch.randn(size, size, device="cuda").to(torch.float8_e4m3fn).t()  # column-major B
+        one = torch.ones((), device="cuda")
+        f = lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        for _ in range(warmup):
+            f()
+        ts = []
+        for _ in range(max(10, steps // 4)):
+            flush.zero_()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            f()
+            s1.record()
+            torch.cuda.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        ms = sum(ts) / len(ts)
+        res[f"cublaslt_fp8_{size}_tflops"] = 2.0 * size ** 3 / (ms * 1e-3) / 1e12
+        del a, b
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cublas", action="store_true", help="also time cuBLASLt FP8 on the same shape")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

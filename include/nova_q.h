@@ -6,7 +6,8 @@
  * an nq_status_t, and is implemented by hand-written sm_100a CUDA kernels in
  * libnova_q.so.  The C++ API of the reference (FP8GEMM, MinMaxCalibrator,
  * quantize_f32_to_int8, ...) is provided as thin inline shims over these
- * functions in include/nova/quantize/*.hpp.
+ * functions in include/cuda/quantize/*.hpp (same include paths as the
+ * reference).
  *
  * Each declaration names the reference interface it replaces
  * (file:line relative to the pplmx/nova source tree).
@@ -50,7 +51,9 @@ typedef enum {
 } nq_status_t;
 
 typedef enum { NQ_E4M3 = 0, NQ_E5M2 = 1, NQ_INT8 = 2 } nq_format_t;
-typedef enum { NQ_F32 = 0, NQ_BF16 = 1, NQ_S32 = 2 } nq_dtype_t;
+/* NQ_S8: int8 requantized output, clamp(v, +-127) then round half away from
+   zero (QuantizedMatmul::forward, quantize_ops.hpp:73-77). */
+typedef enum { NQ_F32 = 0, NQ_BF16 = 1, NQ_S32 = 2, NQ_S8 = 3 } nq_dtype_t;
 /* B operand layout of a GEMM: NQ_B_KN is K x N row-major (the layout of
    FP8GEMM::forward, fp8_gemm.cu:81); NQ_B_NK is N x K row-major (a
    "packed" weight, the layout of a torch Linear weight). */
@@ -157,8 +160,8 @@ nq_status_t nq_quantize_cols(const float* src, uint8_t* dst, float* scales, int 
  *   tcgen05 kind::i8.
  *   epi(acc) = ((acc * alpha) [* row_scale[m]]) [* col_scale[n]] [+ bias[n]],
  *   each step one fp32 rounding, then converted to out_dtype (NQ_F32,
- *   NQ_BF16 round-to-nearest-even, or NQ_S32 = raw int32 accumulators,
- *   INT8 only).
+ *   NQ_BF16 round-to-nearest-even, NQ_S8 clamp-and-round, or NQ_S32 = raw
+ *   int32 accumulators, INT8 only).
  * Shapes with K % 16, N % 16 or pointers not 16-byte aligned run a SIMT
  * kernel with the same arithmetic. */
 typedef struct {
@@ -191,6 +194,12 @@ nq_status_t nq_fp8_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, 
 nq_status_t nq_fp8e5m2_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k,
                                     int n, float scale_a, float scale_b, float scale_out,
                                     nq_stream_t s);
+/* QuantizedMatmul::mixed_precision, quantize_ops.hpp:83-102 (W8 A32):
+   out[i,j] = sum_p a[i,p] * (b[p,j] * scale_b[p]) in order, one rounding per
+   multiply and add (the reference host loop); all pointers device. */
+nq_status_t nq_mixed_precision_matmul(const float* a, const int8_t* b, const float* scale_b,
+                                      float* out, int m, int k, int n, nq_stream_t s);
+
 /* FP8GEMM::get_workspace_size, fp8_gemm.cu:152-162 (same formula; the
    kernels here need no workspace). */
 size_t nq_fp8_gemm_workspace_size(int m, int k, int n);

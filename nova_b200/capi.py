@@ -17,7 +17,7 @@ if not os.path.exists(LIB_PATH):
 lib = C.CDLL(LIB_PATH)
 
 E4M3, E5M2, INT8 = 0, 1, 2
-F32, BF16, S32 = 0, 1, 2
+F32, BF16, S32, S8 = 0, 1, 2, 3
 B_KN, B_NK = 0, 1
 
 _p, _sz, _f, _i, _u32p = C.c_void_p, C.c_size_t, C.c_float, C.c_int, C.POINTER(C.c_uint32)
@@ -63,6 +63,7 @@ _SIGS = {
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_fp8e5m2_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_device_error_flags": [_u32p, _i],
+    "nq_mixed_precision_matmul": [_p, _p, _p, _p, _i, _i, _i, _p],
 }
 
 lib.nq_status_string.restype = C.c_char_p

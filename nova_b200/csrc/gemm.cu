@@ -62,6 +62,12 @@ __device__ __forceinline__ float epi_value(float acc, float alpha, float rs, con
     return v;
 }
 
+// quantize_ops.hpp:75-77: clamp to [-127, 127], then std::round.
+__device__ __forceinline__ int8_t requant_s8(float v) {
+    v = fmaxf(-127.0f, fminf(127.0f, v));
+    return static_cast<int8_t>(roundf(v));
+}
+
 template <bool INT_ACC>
 __device__ __forceinline__ void store_chunk(const Epi& ep, const uint32_t (&r)[32], int row, int col0, int N,
                                             float rs) {
@@ -83,7 +89,10 @@ __device__ __forceinline__ void store_chunk(const Epi& ep, const uint32_t (&r)[3
         const int col = min(col0 + j, N - 1);  // columns past N are computed but never stored
         v[j] = epi_value(acc, ep.alpha, rs, ep.col_scale, ep.bias, col);
     }
-    if (ep.out_dtype == NQ_BF16) {
+    if (ep.out_dtype == NQ_S8) {
+        int8_t* o = static_cast<int8_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
+        for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = requant_s8(v[j]);
+    } else if (ep.out_dtype == NQ_BF16) {
         uint16_t* o = static_cast<uint16_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
         if (col0 + 32 <= N) {
 #pragma unroll
@@ -303,7 +312,9 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const uint8_t* __restrict__ a
     }
     const float acc = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[0])) : __uint_as_float(r[0]);
     const float v = epi_value(acc, ep.alpha, rs, ep.col_scale, ep.bias, col);
-    if (ep.out_dtype == NQ_BF16)
+    if (ep.out_dtype == NQ_S8)
+        static_cast<int8_t*>(ep.out)[static_cast<size_t>(row) * ep.ldo + col] = requant_s8(v);
+    else if (ep.out_dtype == NQ_BF16)
         static_cast<uint16_t*>(ep.out)[static_cast<size_t>(row) * ep.ldo + col] = static_cast<uint16_t>(f32x2_to_bf16x2(v, 0.0f));
     else
         static_cast<float*>(ep.out)[static_cast<size_t>(row) * ep.ldo + col] = v;
@@ -381,6 +392,23 @@ nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, con
     return NQ_SUCCESS;
 }
 
+// QuantizedMatmul::mixed_precision (quantize_ops.hpp:83-102): one thread per
+// output, the reference's order and roundings (multiply, then add).
+__global__ void __launch_bounds__(256) k_mixed_precision(const float* __restrict__ a, const int8_t* __restrict__ b,
+                                                         const float* __restrict__ scale_b, float* __restrict__ out,
+                                                         int M, int K, int N) {
+    const int col = blockIdx.x * 64 + (threadIdx.x & 63);
+    const int row = blockIdx.y * 4 + (threadIdx.x >> 6);
+    if (row >= M || col >= N) return;
+    const float* ar = a + static_cast<size_t>(row) * K;
+    float s = 0.0f;
+    for (int p = 0; p < K; ++p) {
+        const float bv = __fmul_rn(static_cast<float>(b[static_cast<size_t>(p) * N + col]), __ldg(scale_b + p));
+        s = __fadd_rn(s, __fmul_rn(__ldg(ar + p), bv));
+    }
+    out[static_cast<size_t>(row) * N + col] = s;
+}
+
 }  // namespace
 
 nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, void* out, cudaStream_t s,
@@ -396,7 +424,7 @@ nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, voi
     if (d->a_format < NQ_E4M3 || d->a_format > NQ_INT8 || d->b_format < NQ_E4M3 || d->b_format > NQ_INT8)
         return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: format");
     if (d->b_layout != NQ_B_KN && d->b_layout != NQ_B_NK) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: b_layout");
-    if (d->out_dtype != NQ_F32 && d->out_dtype != NQ_BF16 && !(i8 && d->out_dtype == NQ_S32))
+    if (d->out_dtype != NQ_F32 && d->out_dtype != NQ_BF16 && d->out_dtype != NQ_S8 && !(i8 && d->out_dtype == NQ_S32))
         return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: out_dtype");
     DeviceInfo di;
     nq_status_t st = current_device(&di);
@@ -452,6 +480,22 @@ nq_status_t nq_fp8_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, 
 nq_status_t nq_fp8e5m2_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k, int n, float scale_a,
                                     float scale_b, float scale_out, nq_stream_t s) {
     return fp8_forward(a, b, out, m, k, n, scale_a, scale_b, scale_out, NQ_E5M2, s);
+}
+
+nq_status_t nq_mixed_precision_matmul(const float* a, const int8_t* b, const float* scale_b, float* out, int m, int k,
+                                      int n, nq_stream_t s) {
+    if (m < 0 || k < 0 || n < 0) return nq::fail(NQ_ERROR_INVALID_VALUE, "nq_mixed_precision_matmul: negative size");
+    if (m == 0 || n == 0) return NQ_SUCCESS;
+    if (!out || (k > 0 && (!a || !b || !scale_b)))
+        return nq::fail(NQ_ERROR_INVALID_VALUE, "nq_mixed_precision_matmul: null pointer");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    dim3 grid((n + 63) / 64, (m + 3) / 4);
+    if (grid.y > 65535) return nq::fail(NQ_ERROR_UNSUPPORTED, "nq_mixed_precision_matmul: M too large");
+    nq::k_mixed_precision<<<grid, 256, 0, s>>>(a, b, scale_b, out, m, k, n);
+    NQ_LAUNCH_CHECK("nq_mixed_precision_matmul");
+    return NQ_SUCCESS;
 }
 
 size_t nq_fp8_gemm_workspace_size(int m, int k, int n) {
