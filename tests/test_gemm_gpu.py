@@ -46,7 +46,7 @@ def run_gemm(nq, a, b, m, n, k, fa, fb, b_layout, out_dtype, alpha=1.0, row=None
              simt=False):
     from gpu_util import dev, empty, host, ptr, stream
     d_a, d_b = dev(a), dev(b)
-    esize = 2 if out_dtype == 1 else 4
+    esize = {0: 4, 1: 2, 2: 4, 3: 1}[out_dtype]
     d_o = empty(m * n * esize)
     d_r = dev(row) if row is not None else None
     d_c = dev(col) if col is not None else None
@@ -54,7 +54,7 @@ def run_gemm(nq, a, b, m, n, k, fa, fb, b_layout, out_dtype, alpha=1.0, row=None
     desc = nq.make_desc(m, n, k, fa, fb, b_layout, out_dtype, alpha, ptr(d_r) if d_r is not None else 0,
                         ptr(d_c) if d_c is not None else 0, ptr(d_bi) if d_bi is not None else 0)
     (nq.gemm_simt if simt else nq.gemm)(desc, ptr(d_a), ptr(d_b), ptr(d_o), stream())
-    dt = {0: np.float32, 1: np.uint16, 2: np.int32}[out_dtype]
+    dt = {0: np.float32, 1: np.uint16, 2: np.int32, 3: np.int8}[out_dtype]
     out = host(d_o, dt, (m, n))
     assert nq.device_error_flags() == 0
     return out
@@ -178,3 +178,33 @@ def test_large_fp8_gemm_torch_check(nq):
     err = ((out.double() - ref_bf).abs() / torch.maximum(ref_bf.abs(), 1e-2 * ref_bf.pow(2).mean().sqrt())).max()
     assert float(err) <= FP8_TOL
     assert nq.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(2, 2, 3), (128, 256, 512), (200, 272, 176)])
+def test_int8_requant_epilogue_matches_quantized_matmul(nq, m, n, k):
+    """NQ_S8 epilogue == QuantizedMatmul::forward (quantize_ops.hpp:54-81)."""
+    import oracle_lib as O
+    a, b = int8_operand((m, k), 5), int8_operand((k, n), 6)
+    sa, sb = 0.01, 0.02
+    got = run_gemm(nq, a, b, m, n, k, 2, 2, 0, 3, float(np.float32(sa) * np.float32(sb)))
+    exp = np.empty((m, n), np.int8)
+    O.lib.orc_quantized_matmul(O.ptr(a), O.ptr(b), O.ptr(exp), m, k, n, sa, sb)
+    np.testing.assert_array_equal(got, exp)
+
+
+def test_mixed_precision_matmul(nq):
+    """QuantizedMatmul::mixed_precision (quantize_ops.hpp:83-102): identical
+    roundings to the reference host loop."""
+    from gpu_util import dev, empty, host, ptr, stream
+    m, k, n = 37, 300, 70
+    rng = np.random.default_rng(9)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.integers(-127, 128, (k, n), dtype=np.int8)
+    s = (rng.random(k) * 0.1).astype(np.float32)
+    d_a, d_b, d_s, d_o = dev(a), dev(b), dev(s), empty(4 * m * n)
+    nq.mixed_precision_matmul(ptr(d_a), ptr(d_b), ptr(d_s), ptr(d_o), m, k, n, stream())
+    got = host(d_o, np.float32, (m, n))
+    exp = np.zeros((m, n), np.float32)
+    for p in range(k):
+        exp = (exp + a[:, p:p + 1] * (b[p:p + 1, :].astype(np.float32) * s[p])).astype(np.float32)
+    np.testing.assert_array_equal(got, exp)
