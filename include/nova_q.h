@@ -152,6 +152,23 @@ nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst
 nq_status_t nq_quantize_cols(const float* src, uint8_t* dst, float* scales, int rows, int cols,
                              nq_format_t fmt, nq_stream_t s);
 
+/* Allocation-free twin of nq_quantize_cols, for callers that must not
+   allocate device memory during the call (an engine that owns all of HBM
+   through its own allocator, a plugin host that only hands over input and
+   output buffers, a loop where cudaMalloc's implicit synchronisation is not
+   allowed).  No counterpart in the reference.  Same results as
+   nq_quantize_cols; the per-column amax scratch is a fixed 256 KiB device
+   array inside libnova_q that every GPU loading the library holds until
+   process exit, so cols is limited to 65536 (larger widths return
+   NQ_ERROR_UNSUPPORTED).  The first call on a device looks up that array's
+   address (cudaGetSymbolAddress) with the device current: make that first
+   call before any stream capture.  All calls share the one array, so calls
+   that overlap on the GPU (other streams, other threads) race; serialise
+   them.  Nothing is allocated or freed: the scratch is cleared with
+   cudaMemsetAsync on `s` at the start of every call. */
+nq_status_t nq_quantize_cols_noalloc(const float* src, uint8_t* dst, float* scales, int rows,
+                                     int cols, nq_format_t fmt, nq_stream_t s);
+
 /* ---- GEMM -------------------------------------------------------------------
  * out[m, n] = epi( sum_k A[m, k] * B[k, n] )
  *   A: M x K row-major codes (K-major), B: per b_layout.

@@ -58,6 +58,7 @@ _SIGS = {
     "nq_calibrate_quantize": [_p, _i, _p, _sz, _i, _p, _p],
     "nq_quantize_rows": [_p, _i, _p, _p, _i, _i, _i, _p],
     "nq_quantize_cols": [_p, _p, _p, _i, _i, _i, _p],
+    "nq_quantize_cols_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "nq_gemm": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_gemm_simt": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "codec.cuh"
@@ -524,6 +525,83 @@ nq_status_t nq_quantize_cols(const float* src, uint8_t* dst, float* scales, int 
     }
     nq::scratch_free(amax, s);
     return nq::cuda_status(e, "nq_quantize_cols");
+}
+
+}  // extern "C"
+
+// ---- allocation-free per-column quantize ---------------------------------------
+// Some callers cannot allocate device memory while they run: an engine that
+// reserved all of HBM up front for its own allocator, a plugin host that hands
+// a plugin only its input and output buffers, or a latency-critical loop where
+// cudaMalloc's implicit synchronisation is not allowed.  For them,
+// nq_quantize_cols_noalloc keeps its per-column amax scratch in this fixed
+// array instead of the library's memory pool.  Every GPU that loads the
+// library holds it (65536 x 4 B = 256 KiB) until the process exits.
+static constexpr int kNoAllocMaxCols = 65536;
+static __device__ __align__(256) uint32_t g_noalloc_col_amax[kNoAllocMaxCols];
+
+namespace nq {
+namespace {
+
+// Host code may not pass the symbol itself to a kernel (on the host it names
+// a stand-in, not device memory): its device address is looked up once per
+// device, with that device current, and cached.
+nq_status_t noalloc_scratch(uint32_t** out) {
+    static std::mutex mu;
+    static uint32_t* addr[64] = {};
+    int dev = -1;
+    NQ_CHECK_CUDA(cudaGetDevice(&dev), "nq_quantize_cols_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(NQ_ERROR_NO_DEVICE, "nq_quantize_cols_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_col_amax);
+        if (e != cudaSuccess) return cuda_status(e, "nq_quantize_cols_noalloc: cudaGetSymbolAddress");
+        addr[dev] = static_cast<uint32_t*>(p);
+    }
+    *out = addr[dev];
+    return NQ_SUCCESS;
+}
+}  // namespace
+}  // namespace nq
+
+extern "C" {
+
+nq_status_t nq_quantize_cols_noalloc(const float* src, uint8_t* dst, float* scales, int rows, int cols,
+                                     nq_format_t fmt, nq_stream_t s) {
+    if (rows < 0 || cols < 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_cols_noalloc: negative size");
+    if (cols > kNoAllocMaxCols)
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_quantize_cols_noalloc: cols = " + std::to_string(cols) +
+                                              " exceeds the fixed scratch of " + std::to_string(kNoAllocMaxCols) +
+                                              " columns; use nq_quantize_cols");
+    if (rows == 0 || cols == 0) return NQ_SUCCESS;
+    if (!src || !dst || !scales) return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_cols_noalloc: null pointer");
+    if (fmt != NQ_E4M3 && fmt != NQ_E5M2 && fmt != NQ_INT8)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_cols_noalloc: format");
+    nq::DeviceInfo di;
+    nq_status_t st = nq::current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    uint32_t* amax = nullptr;
+    st = nq::noalloc_scratch(&amax);
+    if (st != NQ_SUCCESS) return st;
+    // The array keeps the previous call's maxima: clear the columns used.
+    NQ_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t) * static_cast<size_t>(cols), s),
+                  "nq_quantize_cols_noalloc: clear scratch");
+    const int groups = (cols + 4 * nq::kThreads - 1) / (4 * nq::kThreads);
+    const int chunks = std::max(1, std::min(rows, (di.sm_count * 8 + groups - 1) / groups));
+    const int rpc = (rows + chunks - 1) / chunks;
+    dim3 g1(groups, (rows + rpc - 1) / rpc);
+    nq::k_col_amax<<<g1, nq::kThreads, 0, s>>>(src, rows, cols, rpc, amax);
+    const size_t total = static_cast<size_t>(rows) * cols;
+    const int g2 = static_cast<int>(
+        std::min<size_t>((total + nq::kThreads - 1) / nq::kThreads, static_cast<size_t>(di.sm_count) * 8));
+    switch (fmt) {
+        case NQ_E4M3: nq::k_quant_cols<nq::dev::kE4M3><<<g2, nq::kThreads, 0, s>>>(src, dst, amax, scales, rows, cols); break;
+        case NQ_E5M2: nq::k_quant_cols<nq::dev::kE5M2><<<g2, nq::kThreads, 0, s>>>(src, dst, amax, scales, rows, cols); break;
+        default: nq::k_quant_cols<nq::dev::kINT8><<<g2, nq::kThreads, 0, s>>>(src, dst, amax, scales, rows, cols); break;
+    }
+    NQ_LAUNCH_CHECK("nq_quantize_cols_noalloc");
+    return NQ_SUCCESS;
 }
 
 }  // extern "C"
