@@ -266,10 +266,258 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_arrive(&tempty[acc]);
         }
     }
+    __syncwarp();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------- CTA-pair kernel (cta_group::2, 256 x 256 tiles) ----------------
+// A cluster of two CTAs computes one 256 x 256 tile per step with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=32).  Each CTA TMA-loads its own
+// half of A (128 rows) and its own half of B (128 columns) into its shared
+// memory, so per SM the tensor core reads 32 KB and TMA writes 32 KB per
+// 128-deep k-block -- a third less shared-memory traffic per FLOP than the
+// single-CTA 128 x 256 tile.  The leader CTA (rank 0) issues the MMAs; its
+// `full` barriers count both CTAs' bytes (cta_group::2 loads signal the
+// leader), `empty` and `tfull` are multicast commits to both CTAs, and both
+// CTAs' epilogue warps arrive on the leader's `tempty`.  Each CTA's TMEM holds
+// its 128 rows of the tile.  No TMA multicast.
+constexpr int P_BM = 256, P_BN = 256;
+constexpr int P_STAGES = 6;
+constexpr int P_A_STAGE = 128 * BK;  // 16 KB per CTA
+constexpr int P_B_STAGE = 128 * BK;  // 16 KB per CTA
+// Epilogue staging: per epilogue warp two 4 KB slots, each one 32 x 32 output
+// chunk (rows of 128 B for 4-byte outputs, 64 B for bf16), swizzled so that
+// the row-per-lane writes are bank-conflict free; a TMA store per chunk.
+constexpr int P_EPI_SLOT = 4096;
+constexpr int P_EPI_BYTES = 4 * 2 * P_EPI_SLOT;
+constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
+
+// Writes lane `row`'s 32 values into a swizzled staging slot: 16-byte chunk j
+// of the row lands at chunk j ^ (row & 7) for 128-byte rows (TMA
+// SWIZZLE_128B) or j ^ ((row >> 1) & 3) for 64-byte rows (SWIZZLE_64B).
+template <bool INT_ACC>
+__device__ __forceinline__ void stage_chunk(uint8_t* slot, int row, const uint32_t (&r)[32], const float (&v)[32],
+                                            nq_dtype_t dt) {
+    if (dt == NQ_BF16) {
+        uint8_t* rowp = slot + row * 64;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint4 w;
+            w.x = f32x2_to_bf16x2(v[8 * j], v[8 * j + 1]);
+            w.y = f32x2_to_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            w.z = f32x2_to_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            w.w = f32x2_to_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(rowp + 16 * (j ^ ((row >> 1) & 3))) = w;
+        }
+    } else {
+        uint8_t* rowp = slot + row * 128;
+        const bool raw = INT_ACC && dt == NQ_S32;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            uint4 w;
+            if (raw) {
+                w = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            } else {
+                w = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                               __float_as_uint(v[4 * j + 3]));
+            }
+            *reinterpret_cast<uint4*>(rowp + 16 * (j ^ (row & 7))) = w;
+        }
+    }
+}
+
+template <bool INT8_KIND, bool B_KN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + P_STAGES * P_A_STAGE;
+    uint8_t* sEpi = sB + P_STAGES * P_B_STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + P_EPI_BYTES);
+    uint64_t* full = bars;                  // [P_STAGES] leader: both CTAs' TMA -> MMA
+    uint64_t* empty = bars + P_STAGES;      // [P_STAGES] MMA -> each CTA's producer
+    uint64_t* tfull = bars + 2 * P_STAGES;  // [2] MMA -> each CTA's epilogue
+    uint64_t* tempty = tfull + 2;           // [2] leader: 8 epilogue warps -> MMA
+    uint64_t* done = tempty + 2;            // leader: MMA drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cluster = blockIdx.x >> 1;
+    const int nclusters = gridDim.x >> 1;
+    const int m_tiles = (M + P_BM - 1) / P_BM;
+    const int n_tiles = (N + P_BN - 1) / P_BN;
+    const int num_tiles = m_tiles * n_tiles;
+    const int kblocks = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 8);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        if (ep.out_dtype != NQ_S8) tma_prefetch_desc(&tmC);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (elect_one()) {
+            const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+                const int mb = tile % m_tiles, nb = tile / m_tiles;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_STAGE + P_B_STAGE));
+                    const uint32_t fb = full_leader + 8u * stage;
+                    tma_load_2d_pair(sA + stage * P_A_STAGE, &tmA, fb, kb * BK, mb * P_BM + rank * 128);
+                    if (B_KN) tma_load_2d_pair(sB + stage * P_B_STAGE, &tmB, fb, nb * P_BN + rank * 128, kb * BK);
+                    else tma_load_2d_pair(sB + stage * P_B_STAGE, &tmB, fb, kb * BK, nb * P_BN + rank * 128);
+                    if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // let issued copies land: the free signal of every stage in flight
+                for (int s = 0; s < P_STAGES; ++s) mbar_wait(&empty[s], phase ^ 1u, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader CTA only) ----------------
+        if (rank == 0 && elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;
+            for (int tile = cluster; tile < num_tiles && ok; tile += nclusters, ++it) {
+                const int acc = it & 1;
+                const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + stage * P_A_STAGE);
+                    const uint32_t b_addr = smem_u32(sB + stage * P_B_STAGE);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk) {
+                        // per CTA: A is 128 K-major rows; B is 128 columns,
+                        // MN-major (K x N source) or K-major (N x K source)
+                        const uint64_t adesc = smem_desc_sw128(a_addr + 32u * kk, 16u, 1024u);
+                        const uint64_t bdesc = B_KN ? smem_desc_sw128(b_addr + 4096u * kk, P_B_STAGE, 1024u)
+                                                    : smem_desc_sw128(b_addr + 32u * kk, 16u, 1024u);
+                        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+                        if (INT8_KIND) mma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
+                        else mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, accum);
+                    }
+                    tc_commit_pair_mc(&empty[stage], 0x3);
+                    if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc_commit_pair_mc(&tfull[acc], 0x3);
+            }
+            tc_commit_pair_mc(done, 0x1);
+            mbar_wait(done, 0, err);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+        const int quarter = warp & 3;
+        const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
+        const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+        const bool tma_out = ep.out_dtype != NQ_S8;
+        uint8_t* slots = sEpi + quarter * 2 * P_EPI_SLOT;
+        int it = 0;
+        int chunk_seq = 0;  // chunks stored by this warp so far (selects the staging slot)
+        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+            const int acc = it & 1;
+            const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
+            bool ok = mbar_wait(&tfull[acc], acc_phase, err);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int mb = tile % m_tiles, nb = tile / m_tiles;
+            const int row = mb * P_BM + row_in_tile;
+            const int row0_warp = mb * P_BM + static_cast<int>(rank) * 128 + quarter * 32;
+            const float rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr, r);
+#pragma unroll 1
+            for (int c = 0; c < P_BN / 32; ++c) {
+                tmem_ld_wait();
+                uint32_t cur[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) cur[j] = r[j];
+                if (c + 1 < P_BN / 32) {
+                    tmem_ld_32x32b_x32(taddr + 32u * (c + 1), r);  // next chunk in flight
+                } else {
+                    // every TMEM column of this accumulator has been read: hand it back
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (rank == 0) mbar_arrive(&tempty[acc]);
+                        else mbar_arrive_remote(tempty_leader + 8u * acc);
+                    }
+                }
+                const int col0 = nb * P_BN + c * 32;
+                if (col0 >= N || row0_warp >= M) continue;
+                if (!tma_out) {
+                    if (row < M) store_chunk<INT8_KIND>(ep, cur, row, col0, N, rs);
+                    continue;
+                }
+                float v[32];
+                if (!(INT8_KIND && ep.out_dtype == NQ_S32)) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(cur[j])) : __uint_as_float(cur[j]);
+                        v[j] = epi_value(a, ep.alpha, rs, ep.col_scale, ep.bias, min(col0 + j, N - 1));
+                    }
+                }
+                uint8_t* slot = slots + (chunk_seq & 1) * P_EPI_SLOT;
+                if (lane == 0) bulk_wait_group_read<1>();  // the store issued two chunks ago has read this slot
+                __syncwarp();
+                stage_chunk<INT8_KIND>(slot, lane, cur, v, ep.out_dtype);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmC, slot, col0, row0_warp);
+                    bulk_commit_group();
+                }
+                ++chunk_seq;
+            }
+        }
+        if (lane == 0) bulk_wait_group_all();
+    }
+    __syncwarp();  // reconverge the producer / MMA warps before the aligned cluster barrier
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -359,31 +607,101 @@ nq_status_t make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
     return NQ_SUCCESS;
 }
 
+// The shared-memory opt-in is a per-device function attribute.
+template <class F>
+nq_status_t ensure_smem_attr(F kern, int bytes, int device, uint64_t* flags) {
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    const uint64_t bit = 1ull << (device & 63);
+    if (!(*flags & bit)) {
+        NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                      "cudaFuncSetAttribute(gemm)");
+        *flags |= bit;
+    }
+    return NQ_SUCCESS;
+}
+
+uint32_t gemm_idesc(const nq_gemm_desc_t& d, bool i8, bool kn, uint32_t m, uint32_t n) {
+    if (i8) return make_idesc(2u, 1u, 1u, kn ? 1u : 0u, m, n);
+    return make_idesc(1u, d.a_format == NQ_E5M2 ? 1u : 0u, d.b_format == NQ_E5M2 ? 1u : 0u, kn ? 1u : 0u, m, n);
+}
+
+// Output map of the TMA-store epilogue: 32 x 32 boxes, swizzled to match
+// stage_chunk (128-byte rows: SWIZZLE_128B, 64-byte bf16 rows: SWIZZLE_64B).
+nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
+    EncodeTiledFn fn;
+    nq_status_t st = get_encode_fn(&fn);
+    if (st != NQ_SUCCESS) return st;
+    const bool bf = d.out_dtype == NQ_BF16;
+    const uint64_t esize = bf ? 2 : 4;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.n), static_cast<cuuint64_t>(d.m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.n) * esize};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                      : (d.out_dtype == NQ_S32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    CUresult r = fn(map, dt, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    bf ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled (output) failed (" + std::to_string(int(r)) + ")");
+    return NQ_SUCCESS;
+}
+
+template <bool I8, bool KN>
+nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, void* out, const Epi& ep,
+                       cudaStream_t s, const DeviceInfo& di) {
+    CUtensorMap ma, mb, mc;
+    nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, 128);
+    if (st != NQ_SUCCESS) return st;
+    if (KN) st = make_map(&mb, b, d.n, d.k, d.n, 128, BK);
+    else st = make_map(&mb, b, d.k, d.n, d.k, BK, 128);
+    if (st != NQ_SUCCESS) return st;
+    if (d.out_dtype != NQ_S8) st = make_out_map(&mc, out, d);
+    else std::memset(&mc, 0, sizeof(mc));
+    if (st != NQ_SUCCESS) return st;
+    const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
+    auto kern = k_gemm_tc2<I8, KN>;
+    static uint64_t attr_set = 0;
+    st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
+    if (st != NQ_SUCCESS) return st;
+    // as many clusters as can be resident at once (an SM without a free partner
+    // in its GPC cannot host half of a pair)
+    static int max_clusters[64] = {};
+    if (!max_clusters[di.device & 63]) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (di.sm_count / 2));
+        cfg.blockDim = dim3(GEMM_THREADS);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        int nc = 0;
+        if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess || nc <= 0) {
+            cudaGetLastError();
+            nc = di.sm_count / 2;
+        }
+        max_clusters[di.device & 63] = nc;
+    }
+    const int tiles = ((d.m + P_BM - 1) / P_BM) * ((d.n + P_BN - 1) / P_BN);
+    const int grid = 2 * std::max(1, std::min(tiles, max_clusters[di.device & 63]));
+    uint32_t* err = device_error_word();
+    kern<<<grid, GEMM_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, err);
+    NQ_LAUNCH_CHECK("nq_gemm (tcgen05, CTA pair)");
+    return NQ_SUCCESS;
+}
+
 template <bool I8, bool KN>
 nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                       const DeviceInfo& di) {
+    if (d.m > BM) return launch_tc2<I8, KN>(d, a, b, ep.out, ep, s, di);
     CUtensorMap ma, mb;
     nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, BM);
     if (st != NQ_SUCCESS) return st;
     if (KN) st = make_map(&mb, b, d.n, d.k, d.n, BN / 2, BK);
     else st = make_map(&mb, b, d.k, d.n, d.k, BK, BN);
     if (st != NQ_SUCCESS) return st;
-    uint32_t idesc;
-    if (I8) idesc = make_idesc(2u, 1u, 1u, KN ? 1u : 0u, BM, BN);
-    else idesc = make_idesc(1u, d.a_format == NQ_E5M2 ? 1u : 0u, d.b_format == NQ_E5M2 ? 1u : 0u, KN ? 1u : 0u, BM, BN);
+    const uint32_t idesc = gemm_idesc(d, I8, KN, BM, BN);
     auto kern = k_gemm_tc<I8, KN>;
-    // The shared-memory opt-in is a per-device function attribute.
     static uint64_t attr_set = 0;
-    static std::mutex mu;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        const uint64_t bit = 1ull << (di.device & 63);
-        if (!(attr_set & bit)) {
-            NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
-                          "cudaFuncSetAttribute(gemm)");
-            attr_set |= bit;
-        }
-    }
+    st = ensure_smem_attr(kern, SMEM_BYTES, di.device, &attr_set);
+    if (st != NQ_SUCCESS) return st;
     const int tiles = ((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
     const int grid = std::max(1, std::min(tiles, di.sm_count));
     uint32_t* err = device_error_word();
