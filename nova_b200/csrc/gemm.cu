@@ -52,6 +52,29 @@ struct Epi {
     const float* bias;
 };
 
+// Per-chunk column operands of the epilogue: lane j holds column (col0 + j)'s
+// scale and bias, or the exact identities 1.0 and -0.0 when absent
+// (x * 1 == x and x + (-0) == x for every x, signed zeros included), so the
+// element loop below runs without branches and its result is bit-identical to
+// the conditional form.
+struct ColOps {
+    float cs, b;
+};
+__device__ __forceinline__ ColOps col_ops(const float* col_scale, const float* bias, int col0, int lane, int N) {
+    const int c = min(col0 + lane, N - 1);
+    ColOps o;
+    o.cs = col_scale ? __ldg(col_scale + c) : 1.0f;
+    o.b = bias ? __ldg(bias + c) : -0.0f;
+    return o;
+}
+// ((acc * alpha) * rs) * cs[j] + b[j], one rounding per step; j's operands
+// are broadcast from lane j.
+__device__ __forceinline__ float epi_elem(float acc, float alpha, float rs, const ColOps& o, int j) {
+    float v = __fmul_rn(__fmul_rn(acc, alpha), rs);
+    v = __fmul_rn(v, __shfl_sync(0xffffffffu, o.cs, j));
+    return __fadd_rn(v, __shfl_sync(0xffffffffu, o.b, j));
+}
+
 // v = ((acc * alpha) [* rs]) [* cs] [+ b]: one rounding per step, never fused.
 __device__ __forceinline__ float epi_value(float acc, float alpha, float rs, const float* col_scale,
                                            const float* bias, int col) {
@@ -68,30 +91,39 @@ __device__ __forceinline__ int8_t requant_s8(float v) {
     return static_cast<int8_t>(roundf(v));
 }
 
+// Called by all 32 lanes together (the column operands are shuffled across
+// the warp); only lanes with row_ok store.
 template <bool INT_ACC>
 __device__ __forceinline__ void store_chunk(const Epi& ep, const uint32_t (&r)[32], int row, int col0, int N,
-                                            float rs) {
+                                            float rs, bool row_ok) {
     if (INT_ACC && ep.out_dtype == NQ_S32) {
+        if (!row_ok) return;
         int32_t* o = static_cast<int32_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
         if (col0 + 32 <= N) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<int4*>(o + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
         } else {
-            for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = static_cast<int32_t>(r[j]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) o[j] = static_cast<int32_t>(r[j]);
         }
         return;
     }
     float v[32];
+    // columns past N are computed (with column N-1's operands) but never stored
+    const ColOps cop = col_ops(ep.col_scale, ep.bias, col0, static_cast<int>(lane_id()), N);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const float acc = INT_ACC ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
-        const int col = min(col0 + j, N - 1);  // columns past N are computed but never stored
-        v[j] = epi_value(acc, ep.alpha, rs, ep.col_scale, ep.bias, col);
+        v[j] = epi_elem(acc, ep.alpha, rs, cop, j);
     }
+    if (!row_ok) return;
     if (ep.out_dtype == NQ_S8) {
         int8_t* o = static_cast<int8_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
-        for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = requant_s8(v[j]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (col0 + j < N) o[j] = requant_s8(v[j]);
     } else if (ep.out_dtype == NQ_BF16) {
         uint16_t* o = static_cast<uint16_t*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
         if (col0 + 32 <= N) {
@@ -105,7 +137,9 @@ __device__ __forceinline__ void store_chunk(const Epi& ep, const uint32_t (&r)[3
                 *reinterpret_cast<uint4*>(o + j) = w;
             }
         } else {
-            for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = static_cast<uint16_t>(f32x2_to_bf16x2(v[j], 0.0f));
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) o[j] = static_cast<uint16_t>(f32x2_to_bf16x2(v[j], 0.0f));
         }
     } else {
         float* o = static_cast<float*>(ep.out) + static_cast<size_t>(row) * ep.ldo + col0;
@@ -113,7 +147,9 @@ __device__ __forceinline__ void store_chunk(const Epi& ep, const uint32_t (&r)[3
 #pragma unroll
             for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         } else {
-            for (int j = 0; j < 32 && col0 + j < N; ++j) o[j] = v[j];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) o[j] = v[j];
         }
     }
 }
@@ -260,7 +296,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 tmem_ld_32x32b_x32(taddr + 32u * c, r);
                 tmem_ld_wait();
                 const int col0 = nb * BN + c * 32;
-                if (row < M && col0 < N) store_chunk<INT8_KIND>(ep, r, row, col0, N, rs);
+                if (col0 < N) store_chunk<INT8_KIND>(ep, r, row, col0, N, rs, row < M);
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
@@ -289,6 +325,42 @@ constexpr int P_BM = 256, P_BN = 256;
 constexpr int P_STAGES = 6;
 constexpr int P_A_STAGE = 128 * BK;  // 16 KB per CTA
 constexpr int P_B_STAGE = 128 * BK;  // 16 KB per CTA
+// Tail split: when the last wave is at most half full, its tiles are cut along
+// K into two parts that run side by side on otherwise idle CTA pairs.  Part 1
+// parks its raw accumulators in `ws` and counts its 8 epilogue warps in
+// `flags`; part 0 waits for them, adds the partial (exact for int32) and
+// writes the tile.
+struct SplitTail {
+    int full_units;   // units [0, full_units) are whole tiles
+    int rem;          // tiles in the tail wave
+    int split;        // K parts per tail tile: 1 (no split) or 2
+    uint32_t* ws;     // [rem][256 x 256] accumulators of part 1
+    uint32_t* flags;  // [rem] arrivals of part 1's 8 epilogue warps
+};
+struct Unit {
+    int tile, part, kb0, kb1;
+};
+__device__ __forceinline__ Unit decode_unit(int u, const SplitTail& st, int kblocks) {
+    if (st.split <= 1 || u < st.full_units) return Unit{u, 0, 0, kblocks};
+    const int v = u - st.full_units;
+    const int part = v / st.rem;
+    return Unit{st.full_units + v % st.rem, part, part * kblocks / st.split, (part + 1) * kblocks / st.split};
+}
+// Spins (bounded) until *flag >= want, reading with acquire semantics.
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t want, uint32_t* err) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.global.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v >= want) return true;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            if (err) atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
 // Epilogue staging: per epilogue warp two 4 KB slots, each one 32 x 32 output
 // chunk (rows of 128 B for 4-byte outputs, 64 B for bf16), swizzled so that
 // the row-per-lane writes are bank-conflict free; a TMA store per chunk.
@@ -296,44 +368,14 @@ constexpr int P_EPI_SLOT = 4096;
 constexpr int P_EPI_BYTES = 4 * 2 * P_EPI_SLOT;
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
 
-// Writes lane `row`'s 32 values into a swizzled staging slot: 16-byte chunk j
-// of the row lands at chunk j ^ (row & 7) for 128-byte rows (TMA
-// SWIZZLE_128B) or j ^ ((row >> 1) & 3) for 64-byte rows (SWIZZLE_64B).
-template <bool INT_ACC>
-__device__ __forceinline__ void stage_chunk(uint8_t* slot, int row, const uint32_t (&r)[32], const float (&v)[32],
-                                            nq_dtype_t dt) {
-    if (dt == NQ_BF16) {
-        uint8_t* rowp = slot + row * 64;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint4 w;
-            w.x = f32x2_to_bf16x2(v[8 * j], v[8 * j + 1]);
-            w.y = f32x2_to_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-            w.z = f32x2_to_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-            w.w = f32x2_to_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-            *reinterpret_cast<uint4*>(rowp + 16 * (j ^ ((row >> 1) & 3))) = w;
-        }
-    } else {
-        uint8_t* rowp = slot + row * 128;
-        const bool raw = INT_ACC && dt == NQ_S32;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            uint4 w;
-            if (raw) {
-                w = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-            } else {
-                w = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
-                               __float_as_uint(v[4 * j + 3]));
-            }
-            *reinterpret_cast<uint4*>(rowp + 16 * (j ^ (row & 7))) = w;
-        }
-    }
-}
 
-template <bool INT8_KIND, bool B_KN>
+// OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
+// 1 = bf16 through TMA stores, 2 = int8 requantized, direct stores.
+template <bool INT8_KIND, bool B_KN, int OUTK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, uint32_t* err) {
+               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
+               uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -356,6 +398,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     const int n_tiles = (N + P_BN - 1) / P_BN;
     const int num_tiles = m_tiles * n_tiles;
     const int kblocks = (K + BK - 1) / BK;
+    const int num_units = st.split > 1 ? st.full_units + st.rem * st.split : num_tiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
@@ -372,7 +415,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
-        if (ep.out_dtype != NQ_S8) tma_prefetch_desc(&tmC);
+        if (OUTK != 2) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -390,9 +433,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
-                const int mb = tile % m_tiles, nb = tile / m_tiles;
-                for (int kb = 0; kb < kblocks; ++kb) {
+            for (int u = cluster; u < num_units && ok; u += nclusters) {
+                const Unit un = decode_unit(u, st, kblocks);
+                const int mb = un.tile % m_tiles, nb = un.tile / m_tiles;
+                for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
                     if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_STAGE + P_B_STAGE));
                     const uint32_t fb = full_leader + 8u * stage;
@@ -414,13 +458,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             uint32_t phase = 0;
             bool ok = true;
             int it = 0;
-            for (int tile = cluster; tile < num_tiles && ok; tile += nclusters, ++it) {
+            for (int u = cluster; u < num_units && ok; u += nclusters, ++it) {
+                const Unit un = decode_unit(u, st, kblocks);
                 const int acc = it & 1;
                 const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait(&full[stage], phase, err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + stage * P_A_STAGE);
@@ -432,7 +477,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                         const uint64_t adesc = smem_desc_sw128(a_addr + 32u * kk, 16u, 1024u);
                         const uint64_t bdesc = B_KN ? smem_desc_sw128(b_addr + 4096u * kk, P_B_STAGE, 1024u)
                                                     : smem_desc_sw128(b_addr + 32u * kk, 16u, 1024u);
-                        const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t accum = (kb > un.kb0 || kk > 0) ? 1u : 0u;
                         if (INT8_KIND) mma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
                         else mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, accum);
                     }
@@ -449,11 +494,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         const int quarter = warp & 3;
         const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
         const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
-        const bool tma_out = ep.out_dtype != NQ_S8;
         uint8_t* slots = sEpi + quarter * 2 * P_EPI_SLOT;
+        const bool raw_s32 = INT8_KIND && OUTK == 0 && ep.out_dtype == NQ_S32;
         int it = 0;
         int chunk_seq = 0;  // chunks stored by this warp so far (selects the staging slot)
-        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+        for (int u = cluster; u < num_units; u += nclusters, ++it) {
+            const Unit un = decode_unit(u, st, kblocks);
+            const int tile = un.tile;
             const int acc = it & 1;
             const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
             bool ok = mbar_wait(&tfull[acc], acc_phase, err);
@@ -461,19 +508,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             tc_fence_after();
             const int mb = tile % m_tiles, nb = tile / m_tiles;
             const int row = mb * P_BM + row_in_tile;
+            const bool split_tile = st.split > 1 && tile >= st.full_units;
+            const int slot_id = tile - st.full_units;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
+            // the other K part of a split tile (one partial: split == 2)
+            uint32_t* wsp = split_tile ? st.ws + static_cast<size_t>(slot_id) * (P_BM * P_BN) +
+                                             static_cast<size_t>(row_in_tile) * P_BN
+                                       : nullptr;
+            if (split_tile && un.part > 0) {
+                // part 1 of a tail tile: park the raw accumulators for part 0
+#pragma unroll 1
+                for (int c = 0; c < P_BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + 32u * c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        __stcg(reinterpret_cast<uint4*>(wsp + c * 32 + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+                }
+                tc_fence_before();
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) {
+                    if (rank == 0) mbar_arrive(&tempty[acc]);
+                    else mbar_arrive_remote(tempty_leader + 8u * acc);
+                    atomicAdd(st.flags + slot_id, 1u);
+                }
+                continue;
+            }
+            if (split_tile) {
+                // part 0: wait (bounded) until part 1's 8 warps have parked their rows
+                if (lane == 0) wait_flag_geq(st.flags + slot_id, 8u, err);
+                __syncwarp();
+            }
             const int row0_warp = mb * P_BM + static_cast<int>(rank) * 128 + quarter * 32;
             const float rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
             uint32_t r[32];
+            uint4 w[8];
             tmem_ld_32x32b_x32(taddr, r);
+            if (split_tile) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp) + j);
+            }
 #pragma unroll 1
             for (int c = 0; c < P_BN / 32; ++c) {
                 tmem_ld_wait();
                 uint32_t cur[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) cur[j] = r[j];
+                if (split_tile) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t q[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int e = 4 * j + t;
+                            if (INT8_KIND) cur[e] = static_cast<uint32_t>(static_cast<int32_t>(cur[e]) + static_cast<int32_t>(q[t]));
+                            else cur[e] = __float_as_uint(__fadd_rn(__uint_as_float(cur[e]), __uint_as_float(q[t])));
+                        }
+                    }
+                }
                 if (c + 1 < P_BN / 32) {
                     tmem_ld_32x32b_x32(taddr + 32u * (c + 1), r);  // next chunk in flight
+                    if (split_tile) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp + (c + 1) * 32) + j);
+                    }
                 } else {
                     // every TMEM column of this accumulator has been read: hand it back
                     tc_fence_before();
@@ -485,22 +585,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 }
                 const int col0 = nb * P_BN + c * 32;
                 if (col0 >= N || row0_warp >= M) continue;
-                if (!tma_out) {
-                    if (row < M) store_chunk<INT8_KIND>(ep, cur, row, col0, N, rs);
+                if (OUTK == 2) {
+                    store_chunk<INT8_KIND>(ep, cur, row, col0, N, rs, row < M);
                     continue;
-                }
-                float v[32];
-                if (!(INT8_KIND && ep.out_dtype == NQ_S32)) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(cur[j])) : __uint_as_float(cur[j]);
-                        v[j] = epi_value(a, ep.alpha, rs, ep.col_scale, ep.bias, min(col0 + j, N - 1));
-                    }
                 }
                 uint8_t* slot = slots + (chunk_seq & 1) * P_EPI_SLOT;
                 if (lane == 0) bulk_wait_group_read<1>();  // the store issued two chunks ago has read this slot
                 __syncwarp();
-                stage_chunk<INT8_KIND>(slot, lane, cur, v, ep.out_dtype);
+                const ColOps cop = col_ops(ep.col_scale, ep.bias, col0, lane, N);
+                if (OUTK == 1) {
+                    // bf16: 64-byte rows, 16-byte chunk j at j ^ ((row >> 1) & 3)
+                    uint8_t* rowp = slot + lane * 64;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float v[8];
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            const int e = 8 * j + t;
+                            const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(cur[e])) : __uint_as_float(cur[e]);
+                            v[t] = epi_elem(a, ep.alpha, rs, cop, e);
+                        }
+                        uint4 q;
+                        q.x = f32x2_to_bf16x2(v[0], v[1]);
+                        q.y = f32x2_to_bf16x2(v[2], v[3]);
+                        q.z = f32x2_to_bf16x2(v[4], v[5]);
+                        q.w = f32x2_to_bf16x2(v[6], v[7]);
+                        *reinterpret_cast<uint4*>(rowp + 16 * (j ^ ((lane >> 1) & 3))) = q;
+                    }
+                } else {
+                    // 4-byte values: 128-byte rows, 16-byte chunk j at j ^ (row & 7)
+                    uint8_t* rowp = slot + lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        uint4 q;
+                        if (raw_s32) {
+                            q = make_uint4(cur[4 * j], cur[4 * j + 1], cur[4 * j + 2], cur[4 * j + 3]);
+                        } else {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                const int e = 4 * j + t;
+                                const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(cur[e])) : __uint_as_float(cur[e]);
+                                o[t] = __float_as_uint(epi_elem(a, ep.alpha, rs, cop, e));
+                            }
+                            q = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
+                        *reinterpret_cast<uint4*>(rowp + 16 * (j ^ (lane & 7))) = q;
+                    }
+                }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -627,7 +759,8 @@ uint32_t gemm_idesc(const nq_gemm_desc_t& d, bool i8, bool kn, uint32_t m, uint3
 }
 
 // Output map of the TMA-store epilogue: 32 x 32 boxes, swizzled to match
-// stage_chunk (128-byte rows: SWIZZLE_128B, 64-byte bf16 rows: SWIZZLE_64B).
+// the epilogue's staging layout (128-byte rows: SWIZZLE_128B, 64-byte bf16 rows:
+// SWIZZLE_64B).
 nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
     EncodeTiledFn fn;
     nq_status_t st = get_encode_fn(&fn);
@@ -647,7 +780,7 @@ nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
     return NQ_SUCCESS;
 }
 
-template <bool I8, bool KN>
+template <bool I8, bool KN, int OUTK>
 nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, void* out, const Epi& ep,
                        cudaStream_t s, const DeviceInfo& di) {
     CUtensorMap ma, mb, mc;
@@ -660,7 +793,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     else std::memset(&mc, 0, sizeof(mc));
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
-    auto kern = k_gemm_tc2<I8, KN>;
+    auto kern = k_gemm_tc2<I8, KN, OUTK>;
     static uint64_t attr_set = 0;
     st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
@@ -680,17 +813,45 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
         max_clusters[di.device & 63] = nc;
     }
     const int tiles = ((d.m + P_BM - 1) / P_BM) * ((d.n + P_BN - 1) / P_BN);
-    const int grid = 2 * std::max(1, std::min(tiles, max_clusters[di.device & 63]));
+    const int clusters = std::max(1, std::min(tiles, max_clusters[di.device & 63]));
+    const int grid = 2 * clusters;
+    const int kblocks = (d.k + BK - 1) / BK;
+    SplitTail tail{tiles, 0, 1, nullptr, nullptr};
+    const int rem = tiles % clusters;
+    // Splitting pays off only when a tile's MMA time clearly exceeds its
+    // epilogue (part 0's epilogue waits for part 1's): long K only.
+    const int split = (rem && clusters / rem >= 2 && kblocks >= 48) ? 2 : 1;
+    void* scratch = nullptr;
+    if (split >= 2) {
+        tail.full_units = tiles - rem;
+        tail.rem = rem;
+        tail.split = split;
+        const size_t ws_bytes = static_cast<size_t>(rem) * P_BM * P_BN * 4;
+        st = scratch_alloc(&scratch, ws_bytes + 256 * ((rem * 4 + 255) / 256), s);
+        if (st != NQ_SUCCESS) return st;
+        tail.ws = static_cast<uint32_t*>(scratch);
+        tail.flags = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + ws_bytes);
+        cudaError_t e = cudaMemsetAsync(tail.flags, 0, sizeof(uint32_t) * rem, s);
+        if (e != cudaSuccess) {
+            scratch_free(scratch, s);
+            return cuda_status(e, "nq_gemm: clear split flags");
+        }
+    }
     uint32_t* err = device_error_word();
-    kern<<<grid, GEMM_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, err);
-    NQ_LAUNCH_CHECK("nq_gemm (tcgen05, CTA pair)");
-    return NQ_SUCCESS;
+    kern<<<grid, GEMM_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, err);
+    cudaError_t e = cudaGetLastError();
+    if (scratch) scratch_free(scratch, s);
+    return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
 }
 
 template <bool I8, bool KN>
 nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                       const DeviceInfo& di) {
-    if (d.m > BM) return launch_tc2<I8, KN>(d, a, b, ep.out, ep, s, di);
+    if (d.m > BM) {
+        if (d.out_dtype == NQ_BF16) return launch_tc2<I8, KN, 1>(d, a, b, ep.out, ep, s, di);
+        if (d.out_dtype == NQ_S8) return launch_tc2<I8, KN, 2>(d, a, b, ep.out, ep, s, di);
+        return launch_tc2<I8, KN, 0>(d, a, b, ep.out, ep, s, di);
+    }
     CUtensorMap ma, mb;
     nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, BM);
     if (st != NQ_SUCCESS) return st;

@@ -208,3 +208,38 @@ def test_mixed_precision_matmul(nq):
     for p in range(k):
         exp = (exp + a[:, p:p + 1] * (b[p:p + 1, :].astype(np.float32) * s[p])).astype(np.float32)
     np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("m,n,k,b_layout", [(2560, 2048, 1024, 0), (2560, 2048, 1024, 1), (4352, 4096, 512, 0),
+                                            (8192, 14336, 256, 1)])
+def test_tail_split_int8_exact_vs_torch(nq, m, n, k, b_layout):
+    """Shapes with more 256x256 tiles than CTA pairs: the last wave's tiles
+    are split along K across pairs; int32 partial sums must still be exact.
+    Checked against torch._int_mm (exact int32 accumulation)."""
+    import torch
+    from gpu_util import stream
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+    b = torch.randint(-127, 128, (k, n) if b_layout == 0 else (n, k), dtype=torch.int8, device="cuda", generator=g)
+    out = torch.empty(m, n, dtype=torch.int32, device="cuda")
+    desc = nq.make_desc(m, n, k, 2, 2, b_layout, 2, 1.0)
+    nq.gemm(desc, a.data_ptr(), b.data_ptr(), out.data_ptr(), stream())
+    ref = torch._int_mm(a, b if b_layout == 0 else b.t().contiguous())
+    assert torch.equal(out, ref)
+    assert nq.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(2560, 2048, 1024), (8192, 14336, 512)])
+def test_tail_split_fp8_vs_torch(nq, m, n, k):
+    import torch
+    from gpu_util import stream
+    g = torch.Generator(device="cuda").manual_seed(7)
+    qa = (torch.randn(m, k, device="cuda", generator=g) * 50).to(torch.float8_e4m3fn)
+    qb = (torch.randn(k, n, device="cuda", generator=g) * 50).to(torch.float8_e4m3fn)
+    out = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    desc = nq.make_desc(m, n, k, 0, 0, 0, 0, 1e-3)
+    nq.gemm(desc, qa.data_ptr(), qb.data_ptr(), out.data_ptr(), stream())
+    ref = (qa.double() @ qb.double()) * 1e-3
+    err = ((out.double() - ref).abs() / torch.maximum(ref.abs(), 1e-2 * ref.pow(2).mean().sqrt())).max()
+    assert float(err) <= FP8_TOL_F32_OBSERVED
+    assert nq.device_error_flags() == 0
