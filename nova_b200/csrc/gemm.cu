@@ -322,7 +322,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // CTAs' epilogue warps arrive on the leader's `tempty`.  Each CTA's TMEM holds
 // its 128 rows of the tile.  No TMA multicast.
 constexpr int P_BM = 256, P_BN = 256;
-constexpr int P_STAGES = 6;
+constexpr int P_STAGES = 5;
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue: two warps per
+// TMEM lane quarter, each draining 128 of the tile's 256 columns
+constexpr int P_THREADS = 320;
+constexpr int P_EPI_WARPS = 8;
 constexpr int P_A_STAGE = 128 * BK;  // 16 KB per CTA
 constexpr int P_B_STAGE = 128 * BK;  // 16 KB per CTA
 // Tail split: when the last wave is at most half full, its tiles are cut along
@@ -365,14 +369,14 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t wan
 // chunk (rows of 128 B for 4-byte outputs, 64 B for bf16), swizzled so that
 // the row-per-lane writes are bank-conflict free; a TMA store per chunk.
 constexpr int P_EPI_SLOT = 4096;
-constexpr int P_EPI_BYTES = 4 * 2 * P_EPI_SLOT;
+constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_SLOT;
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
 
 
 // OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
 // 1 = bf16 through TMA stores, 2 = int8 requantized, direct stores.
 template <bool INT8_KIND, bool B_KN, int OUTK>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
                uint32_t* err) {
@@ -385,7 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* full = bars;                  // [P_STAGES] leader: both CTAs' TMA -> MMA
     uint64_t* empty = bars + P_STAGES;      // [P_STAGES] MMA -> each CTA's producer
     uint64_t* tfull = bars + 2 * P_STAGES;  // [2] MMA -> each CTA's epilogue
-    uint64_t* tempty = tfull + 2;           // [2] leader: 8 epilogue warps -> MMA
+    uint64_t* tempty = tfull + 2;           // [2] leader: 16 epilogue warps -> MMA
     uint64_t* done = tempty + 2;            // leader: MMA drain
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
@@ -407,7 +411,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 8);
+            mbar_init(&tempty[a], 2 * P_EPI_WARPS);
         }
         mbar_init(done, 1);
         fence_mbar_init();
@@ -490,11 +494,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             mbar_wait(done, 0, err);
         }
     } else {
-        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
-        const int quarter = warp & 3;
+        // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
+        const int quarter = warp & 3;            // TMEM lanes [32 * quarter, +32)
+        const int colh = (warp - 2) >> 2;        // columns [128 * colh, +128)
         const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
         const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
-        uint8_t* slots = sEpi + quarter * 2 * P_EPI_SLOT;
+        uint8_t* slots = sEpi + (warp - 2) * 2 * P_EPI_SLOT;
         const bool raw_s32 = INT8_KIND && OUTK == 0 && ep.out_dtype == NQ_S32;
         int it = 0;
         int chunk_seq = 0;  // chunks stored by this warp so far (selects the staging slot)
@@ -510,15 +515,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             const int row = mb * P_BM + row_in_tile;
             const bool split_tile = st.split > 1 && tile >= st.full_units;
             const int slot_id = tile - st.full_units;
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * P_BN + colh * 128);
             // the other K part of a split tile (one partial: split == 2)
             uint32_t* wsp = split_tile ? st.ws + static_cast<size_t>(slot_id) * (P_BM * P_BN) +
-                                             static_cast<size_t>(row_in_tile) * P_BN
+                                             static_cast<size_t>(row_in_tile) * P_BN + colh * 128
                                        : nullptr;
             if (split_tile && un.part > 0) {
                 // part 1 of a tail tile: park the raw accumulators for part 0
 #pragma unroll 1
-                for (int c = 0; c < P_BN / 32; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + 32u * c, r);
                     tmem_ld_wait();
@@ -537,12 +543,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 continue;
             }
             if (split_tile) {
-                // part 0: wait (bounded) until part 1's 8 warps have parked their rows
-                if (lane == 0) wait_flag_geq(st.flags + slot_id, 8u, err);
+                // part 0: wait (bounded) until part 1's 16 warps have parked their rows
+                if (lane == 0) wait_flag_geq(st.flags + slot_id, 2u * P_EPI_WARPS, err);
                 __syncwarp();
             }
             const int row0_warp = mb * P_BM + static_cast<int>(rank) * 128 + quarter * 32;
             const float rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+            // this warp's 128 columns, 32 per tcgen05.ld, the next 32 in flight
             uint32_t r[32];
             uint4 w[8];
             tmem_ld_32x32b_x32(taddr, r);
@@ -551,11 +558,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp) + j);
             }
 #pragma unroll 1
-            for (int c = 0; c < P_BN / 32; ++c) {
+            for (int c = 0; c < 4; ++c) {
                 tmem_ld_wait();
                 uint32_t cur[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) cur[j] = r[j];
+                if (c + 1 < 4) {
+                    tmem_ld_32x32b_x32(taddr + 32u * (c + 1), r);  // next chunk in flight
+                } else {
+                    // this warp's TMEM columns have all been read: hand them back
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (rank == 0) mbar_arrive(&tempty[acc]);
+                        else mbar_arrive_remote(tempty_leader + 8u * acc);
+                    }
+                }
                 if (split_tile) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
@@ -568,22 +586,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                         }
                     }
                 }
-                if (c + 1 < P_BN / 32) {
-                    tmem_ld_32x32b_x32(taddr + 32u * (c + 1), r);  // next chunk in flight
-                    if (split_tile) {
+                if (split_tile && c + 1 < 4) {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp + (c + 1) * 32) + j);
-                    }
-                } else {
-                    // every TMEM column of this accumulator has been read: hand it back
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (rank == 0) mbar_arrive(&tempty[acc]);
-                        else mbar_arrive_remote(tempty_leader + 8u * acc);
-                    }
+                    for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp + (c + 1) * 32) + j);
                 }
-                const int col0 = nb * P_BN + c * 32;
+                const int col0 = nb * P_BN + colh * 128 + c * 32;
                 if (col0 >= N || row0_warp >= M) continue;
                 if (OUTK == 2) {
                     store_chunk<INT8_KIND>(ep, cur, row, col0, N, rs, row < M);
@@ -803,7 +810,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     if (!max_clusters[di.device & 63]) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (di.sm_count / 2));
-        cfg.blockDim = dim3(GEMM_THREADS);
+        cfg.blockDim = dim3(P_THREADS);
         cfg.dynamicSmemBytes = P_SMEM_BYTES;
         int nc = 0;
         if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess || nc <= 0) {
@@ -838,7 +845,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
         }
     }
     uint32_t* err = device_error_word();
-    kern<<<grid, GEMM_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, err);
+    kern<<<grid, P_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, err);
     cudaError_t e = cudaGetLastError();
     if (scratch) scratch_free(scratch, s);
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
