@@ -308,10 +308,59 @@ def run_ours(args):
     }
     if args.cublas:
         line["library_comparison"] = cublaslt_fp8(args.steps, args.warmup, flush)
+    if not args.no_secondary:
+        line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"])}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
     return 0
+
+
+def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20)):
+    """HBM-bound kernels of the path at the sweep sizes (fp32 input ~N(0,1)).
+    Algorithmic bytes: quantize 5 B/elem (4 read + 1 write), amax 4 B/elem,
+    calibrate+quantize 5 B/elem compulsory (9 B/elem as two passes), dequant
+    5 B/elem, bf16 per-token quantize 3 B/elem + 4 B/row."""
+    import torch
+    import nova_b200.capi as nq
+    s = torch.cuda.current_stream().cuda_stream
+    out = []
+    for n in sizes:
+        x = torch.randn(n, device="cuda")
+        q = torch.empty(n, dtype=torch.uint8, device="cuda")
+        y = torch.empty(n, device="cuda")
+        sc = torch.empty(2, device="cuda")
+        nq.amax_scale_async(x.data_ptr(), nq.F32, n, nq.E4M3, sc.data_ptr(), s)
+        cols = 4096
+        rows = n // cols
+        xb = x[: rows * cols].view(rows, cols).to(torch.bfloat16)
+        rs = torch.empty(rows, device="cuda")
+        cases = [
+            ("quantize_f32_to_e4m3 (device scale)", 5.0, lambda: nq.quantize_scaled(x.data_ptr(), nq.F32, q.data_ptr(), n, nq.E4M3, sc.data_ptr() + 4, s)),
+            ("quantize_f32_to_int8 (reference API)", 5.0, lambda: nq.quantize_f32_to_int8(x.data_ptr(), q.data_ptr(), n, 0.02, 0.0, 1, s)),
+            ("quantize_f32_to_fp8e4m3 (reference codec)", 5.0, lambda: nq.quantize_f32_to_fp8e4m3(x.data_ptr(), q.data_ptr(), n, s)),
+            ("amax+scale", 4.0, lambda: nq.amax_scale_async(x.data_ptr(), nq.F32, n, nq.E4M3, sc.data_ptr(), s)),
+            ("calibrate+quantize (2 launches)", 5.0, lambda: nq.calibrate_quantize(x.data_ptr(), nq.F32, q.data_ptr(), n, nq.E4M3, sc.data_ptr(), s)),
+            ("dequantize_int8_to_f32", 5.0, lambda: nq.dequantize_int8_to_f32(q.data_ptr(), y.data_ptr(), n, 0.02, 0.0, 1, s)),
+            ("per-token quantize bf16 -> e4m3 (4096 cols)", 3.0, lambda: nq.quantize_rows(xb.data_ptr(), nq.BF16, q.data_ptr(), rs.data_ptr(), rows, cols, nq.E4M3, s)),
+        ]
+        for name, bpe, fn in cases:
+            for _ in range(3):
+                fn()
+            reps = 20 if n <= (1 << 20) else 5
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            gbs = bpe * n / (ms * 1e-3) / 1e9
+            out.append({"kernel": name, "n": n, "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                        "frac_hbm": round(gbs / hbm_gbs, 3)})
+        del x, q, y, xb
+    return out
 
 
 def cublaslt_fp8(steps, warmup, flush):
@@ -350,6 +399,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cublas", action="store_true", help="also time cuBLASLt FP8 on the same shape")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the quantize bandwidth sweep")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

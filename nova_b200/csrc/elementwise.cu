@@ -171,21 +171,31 @@ struct DecOcp {
     __device__ float operator()(uint32_t c) const { return dev::ocp_decode2<F>(c).x * scale; }
 };
 
+// Writes are four times the reads: each lane turns 4 codes (one 4-byte load)
+// into one float4 store, so every warp store instruction covers 512
+// contiguous bytes; four groups per step keep loads in flight.
 template <class Op>
 __global__ void __launch_bounds__(256) k_dequant(const uint8_t* __restrict__ src,
                                                  float* __restrict__ dst, size_t n, int vec, Op op) {
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const size_t nvec = vec ? n / 16 : 0;
-    for (size_t v = t0; v < nvec; v += stride) {
-        uint32_t c[16];
-        load16_codes(src + v * 16, c);
-        float y[16];
+    const size_t ng = vec ? n / 4 : 0;
+    const uint32_t* s4 = reinterpret_cast<const uint32_t*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    size_t g = t0;
+    for (; g + 3 * stride < ng; g += 4 * stride) {
+        uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) y[i] = op(c[i]);
-        store16(dst + v * 16, y);
+        for (int u = 0; u < 4; ++u) w[u] = __ldg(s4 + g + u * stride);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            d4[g + u * stride] = make_float4(op(w[u] & 0xFFu), op((w[u] >> 8) & 0xFFu), op((w[u] >> 16) & 0xFFu), op(w[u] >> 24));
     }
-    for (size_t i = nvec * 16 + t0; i < n; i += stride) dst[i] = op(__ldg(src + i));
+    for (; g < ng; g += stride) {
+        const uint32_t w = __ldg(s4 + g);
+        d4[g] = make_float4(op(w & 0xFFu), op((w >> 8) & 0xFFu), op((w >> 16) & 0xFFu), op(w >> 24));
+    }
+    for (size_t i = ng * 4 + t0; i < n; i += stride) dst[i] = op(__ldg(src + i));
 }
 
 template <class Op>

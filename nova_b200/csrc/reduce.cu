@@ -234,6 +234,53 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows(const In* __restrict__ 
         out[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(ld1(row + i) / s, 0.0f) & 0xFFu);
 }
 
+// Per-row scaled quantize with the row held in registers: one read of the
+// row from HBM.  Each thread owns up to VPT 16-byte vectors (8 bf16 or 4 fp32
+// values each) of the row; cols * sizeof(In) must be a multiple of 16 and at
+// most VPT * 16 * blockDim.x bytes.
+template <int F, class In, int VPT>
+__global__ void __launch_bounds__(kThreads) k_quant_rows_reg(const In* __restrict__ src, uint8_t* __restrict__ dst,
+                                                             float* __restrict__ scales, int cols) {
+    constexpr int EPV = 16 / sizeof(In);  // elements per vector
+    const size_t r = blockIdx.x;
+    const uint4* row = reinterpret_cast<const uint4*>(src + r * static_cast<size_t>(cols));
+    uint8_t* out = dst + r * static_cast<size_t>(cols);
+    const int nv = cols / EPV;
+    uint4 v[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int idx = threadIdx.x + k * kThreads;
+        v[k] = idx < nv ? __ldg(row + idx) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    auto elem = [](const uint4& q, int e) -> float {
+        const uint32_t w = e < EPV / 4 ? q.x : (e < EPV / 2 ? q.y : (e < 3 * EPV / 4 ? q.z : q.w));
+        if (sizeof(In) == 2) return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
+        return __uint_as_float(w);
+    };
+    float a = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) a = fmaxf(a, fabsf(elem(v[k], e)));
+    a = block_minmax(FLT_MAX, a).y;
+    const float s = a > 0.0f ? a / dev::FmtTraits<F>::qmax : 1.0f;
+    if (threadIdx.x == 0) scales[r] = s;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int idx = threadIdx.x + k * kThreads;
+        if (idx >= nv) break;
+        uint32_t codes[EPV / 2];
+#pragma unroll
+        for (int e = 0; e < EPV; e += 2) codes[e / 2] = dev::ocp_encode2<F>(elem(v[k], e) / s, elem(v[k], e + 1) / s);
+        if (EPV == 8) {
+            *reinterpret_cast<uint2*>(out + idx * 8) =
+                make_uint2(codes[0] | (codes[1] << 16), codes[2] | (codes[3] << 16));
+        } else {
+            *reinterpret_cast<uint32_t*>(out + idx * 4) = codes[0] | (codes[1] << 16);
+        }
+    }
+}
+
 // Per-column amax of a rows x cols matrix: grid.x over column groups of 4 x
 // 256, grid.y over row chunks; partial maxima of |x| (>= 0, so their float bit
 // patterns order like unsigned ints) are merged with atomicMax.
@@ -475,6 +522,34 @@ nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst
     nq_status_t st = nq::current_device(&di);
     if (st != NQ_SUCCESS) return st;
     using namespace nq::dev;
+    // register-resident rows: one HBM read per element
+    const size_t row_bytes = static_cast<size_t>(cols) * (src_dtype == NQ_F32 ? 4 : 2);
+    const bool reg_ok = row_bytes % 16 == 0 && nq::aligned16(src) && row_bytes <= 4u * 16u * nq::kThreads &&
+                        reinterpret_cast<uintptr_t>(dst) % (src_dtype == NQ_F32 ? 4 : 8) == 0;
+    if (reg_ok) {
+        const int vpt_need = static_cast<int>((row_bytes / 16 + nq::kThreads - 1) / nq::kThreads);
+#define NQ_QROWS_REG(F, VPT)                                                                                       \
+    (src_dtype == NQ_F32 ? nq::k_quant_rows_reg<F, float, VPT><<<rows, nq::kThreads, 0, s>>>(                      \
+                               static_cast<const float*>(src), dst, scales, cols)                                  \
+                         : nq::k_quant_rows_reg<F, uint16_t, VPT><<<rows, nq::kThreads, 0, s>>>(                   \
+                               static_cast<const uint16_t*>(src), dst, scales, cols))
+#define NQ_QROWS_REG_F(F)                            \
+    do {                                             \
+        if (vpt_need <= 1) NQ_QROWS_REG(F, 1);       \
+        else if (vpt_need <= 2) NQ_QROWS_REG(F, 2);  \
+        else NQ_QROWS_REG(F, 4);                     \
+    } while (0)
+        switch (fmt) {
+            case NQ_E4M3: NQ_QROWS_REG_F(kE4M3); break;
+            case NQ_E5M2: NQ_QROWS_REG_F(kE5M2); break;
+            case NQ_INT8: NQ_QROWS_REG_F(kINT8); break;
+            default: return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: format");
+        }
+#undef NQ_QROWS_REG_F
+#undef NQ_QROWS_REG
+        NQ_LAUNCH_CHECK("nq_quantize_rows");
+        return NQ_SUCCESS;
+    }
 #define NQ_QROWS(F)                                                                                       \
     (src_dtype == NQ_F32                                                                                  \
          ? nq::k_quant_rows<F, float><<<rows, nq::kThreads, 0, s>>>(static_cast<const float*>(src), dst,  \
