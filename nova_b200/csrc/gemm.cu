@@ -660,6 +660,222 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
 }
 
+// ---------------- decode-shaped kernel (few tokens, many output channels) ----------------
+// For M <= 256 tokens against a large weight the roles are swapped: 128 weight
+// rows form the MMA's M side and the (padded) tokens its N side
+// (tcgen05.mma M=128, N=BT), so one MMA tile covers all tokens.  The work --
+// weight slices of 128 rows times k-blocks, in slice-major order -- is cut into
+// equal contiguous ranges, one per CTA (stream-K), so every SM streams the same
+// number of weight bytes.  A slice inside one range is finished directly.  A
+// slice cut by range boundaries is finished by the CTA holding its first
+// k-block (it reaches that part last): every later CTA touching the slice parks
+// its raw accumulators in its own workspace row and raises its flag, and the
+// owner adds them in CTA order before the epilogue -- no atomics, exact for
+// int32 and deterministic for fp32.
+template <int BT>
+struct DecodeCfg {
+    static constexpr int B_STAGE = BT * BK;
+    // as many stages as fit (up to 8: ~128 KB of weights in flight per SM)
+    static constexpr int STAGES = (200 * 1024) / (A_STAGE + B_STAGE) < 8 ? (200 * 1024) / (A_STAGE + B_STAGE) : 8;
+    static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+    static constexpr uint32_t TMEM = BT <= 16 ? 32 : (BT <= 32 ? 64 : (BT <= 64 ? 128 : (BT <= 128 ? 256 : 512)));
+};
+
+__device__ __forceinline__ long long range_begin(long long total, int c, int G) { return total * c / G; }
+
+template <bool INT8_KIND, bool W_KN, int BT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_decode(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
+                  uint32_t idesc, Epi ep, uint32_t* ws, uint32_t* flags, uint32_t* err) {
+    using Cfg = DecodeCfg<BT>;
+    constexpr int D_STAGES = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sW = smem;
+    uint8_t* sX = smem + D_STAGES * A_STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sX + D_STAGES * Cfg::B_STAGE);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + D_STAGES;
+    uint64_t* tfull = bars + 2 * D_STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    const int kblocks = (K + BK - 1) / BK;
+    const long long total = static_cast<long long>((N + 127) / 128) * kblocks;
+    const long long b0 = range_begin(total, blockIdx.x, G);
+    const long long b1 = range_begin(total, blockIdx.x + 1, G);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < D_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (long long kl = b0; kl < b1; ++kl) {
+                const int slice = static_cast<int>(kl / kblocks), kb = static_cast<int>(kl % kblocks);
+                if (!mbar_wait(&empty[stage], phase ^ 1u, err)) break;
+                mbar_arrive_expect_tx(&full[stage], A_STAGE + Cfg::B_STAGE);
+                if (W_KN) tma_load_2d(sW + stage * A_STAGE, &tmW, &full[stage], slice * 128, kb * BK);
+                else tma_load_2d(sW + stage * A_STAGE, &tmW, &full[stage], kb * BK, slice * 128);
+                tma_load_2d(sX + stage * Cfg::B_STAGE, &tmX, &full[stage], kb * BK, 0);
+                if (++stage == D_STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int seg = 0;
+            bool ok = true;
+            for (long long s0 = b0; s0 < b1 && ok; ++seg) {
+                const int slice = static_cast<int>(s0 / kblocks);
+                const long long s1 = min(b1, static_cast<long long>(slice + 1) * kblocks);
+                const int acc = seg & 1;
+                if (!mbar_wait(&tempty[acc], ((static_cast<uint32_t>(seg) >> 1) & 1u) ^ 1u, err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BT);
+                for (long long kl = s0; kl < s1; ++kl) {
+                    if (!mbar_wait(&full[stage], phase, err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sW + stage * A_STAGE);
+                    const uint32_t b_addr = smem_u32(sX + stage * Cfg::B_STAGE);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk) {
+                        // weights: K-major rows (N x K source) or one 128-wide MN-major chunk (K x N source)
+                        const uint64_t adesc = W_KN ? smem_desc_sw128(a_addr + 4096u * kk, A_STAGE, 1024u)
+                                                    : smem_desc_sw128(a_addr + 32u * kk, 16u, 1024u);
+                        const uint64_t bdesc = smem_desc_sw128(b_addr + 32u * kk, 16u, 1024u);
+                        const uint32_t accum = (kl > s0 || kk > 0) ? 1u : 0u;
+                        if (INT8_KIND) mma_i8(d_tmem, adesc, bdesc, idesc, accum);
+                        else mma_f8f6f4(d_tmem, adesc, bdesc, idesc, accum);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == D_STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+                s0 = s1;
+            }
+            tc_commit(done);
+            mbar_wait(done, 0, err);
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int nl = quarter * 32 + lane;  // weight row within the slice
+        int seg = 0;
+        for (long long s0 = b0; s0 < b1; ++seg) {
+            const int slice = static_cast<int>(s0 / kblocks);
+            const long long slice_end = static_cast<long long>(slice + 1) * kblocks;
+            const long long s1 = min(b1, slice_end);
+            const bool head = (s0 % kblocks) == 0;  // this CTA holds the slice's first k-block
+            const int acc = seg & 1;
+            bool ok = mbar_wait(&tfull[acc], (static_cast<uint32_t>(seg) >> 1) & 1u, err);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BT);
+            uint32_t* mine = ws + static_cast<size_t>(blockIdx.x) * BT * 128;
+            if (!head) {
+                // a later part of a slice owned by an earlier CTA: park it
+#pragma unroll 1
+                for (int c = 0; c < BT; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(taddr + c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) __stcg(mine + (c + j) * 128 + nl, r[j]);
+                }
+                tc_fence_before();
+                mbar_arrive(&tempty[acc]);
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(flags + blockIdx.x, 1u);
+                s0 = s1;
+                continue;
+            }
+            // owner: later CTAs touching this slice (if the range ends inside it)
+            int c_first = blockIdx.x + 1, c_last = blockIdx.x;
+            if (s1 < slice_end) {
+                c_last = c_first;
+                while (c_last + 1 < G && range_begin(total, c_last + 1, G) < slice_end) ++c_last;
+                if (lane == 0)
+                    for (int c = c_first; c <= c_last; ++c) wait_flag_geq(flags + c, 4u, err);
+                __syncwarp();
+            }
+            const int n = slice * 128 + nl;
+            const float cs = ep.col_scale && n < N ? __ldg(ep.col_scale + n) : 1.0f;
+            const float bs = ep.bias && n < N ? __ldg(ep.bias + n) : -0.0f;
+#pragma unroll 1
+            for (int c = 0; c < BT; c += 16) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(taddr + c, r);
+                tmem_ld_wait();
+                for (int cc = c_first; cc <= c_last; ++cc) {
+                    const uint32_t* part = ws + static_cast<size_t>(cc) * BT * 128;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const uint32_t q = __ldcg(part + (c + j) * 128 + nl);
+                        if (INT8_KIND) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + static_cast<int32_t>(q));
+                        else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(q)));
+                    }
+                }
+                if (n < N) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int t = c + j;
+                        if (t >= M) break;
+                        const size_t o = static_cast<size_t>(t) * ep.ldo + n;
+                        if (INT8_KIND && ep.out_dtype == NQ_S32) {
+                            static_cast<int32_t*>(ep.out)[o] = static_cast<int32_t>(r[j]);
+                            continue;
+                        }
+                        const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+                        const float rs = ep.row_scale ? __ldg(ep.row_scale + t) : 1.0f;
+                        const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(a, ep.alpha), rs), cs), bs);
+                        if (ep.out_dtype == NQ_BF16) static_cast<uint16_t*>(ep.out)[o] = static_cast<uint16_t>(f32x2_to_bf16x2(v, 0.0f));
+                        else if (ep.out_dtype == NQ_S8) static_cast<int8_t*>(ep.out)[o] = requant_s8(v);
+                        else static_cast<float*>(ep.out)[o] = v;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            s0 = s1;
+        }
+    }
+    __syncwarp();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::TMEM);
+    }
+}
+
 // ---------------- SIMT kernel (odd shapes) ----------------
 template <bool INT8_KIND>
 __global__ void __launch_bounds__(256) k_gemm_simt(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, int M,
@@ -851,9 +1067,63 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
 }
 
+template <bool I8, bool KN, int BT>
+nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
+                             const DeviceInfo& di) {
+    using Cfg = DecodeCfg<BT>;
+    CUtensorMap mw, mx;
+    // weights (the GEMM's B) are the MMA's A operand, tokens (the GEMM's A) its B operand
+    nq_status_t st = KN ? make_map(&mw, b, d.n, d.k, d.n, 128, BK) : make_map(&mw, b, d.k, d.n, d.k, BK, 128);
+    if (st != NQ_SUCCESS) return st;
+    st = make_map(&mx, a, d.k, d.m, d.k, BK, BT);
+    if (st != NQ_SUCCESS) return st;
+    const uint32_t idesc = I8 ? make_idesc(2u, 1u, 1u, 0u, 128u, BT, KN ? 1u : 0u)
+                              : make_idesc(1u, d.b_format == NQ_E5M2 ? 1u : 0u, d.a_format == NQ_E5M2 ? 1u : 0u, 0u,
+                                           128u, BT, KN ? 1u : 0u);
+    auto kern = k_gemm_decode<I8, KN, BT>;
+    static uint64_t attr_set = 0;
+    st = ensure_smem_attr(kern, Cfg::SMEM, di.device, &attr_set);
+    if (st != NQ_SUCCESS) return st;
+    const long long total = static_cast<long long>((d.n + 127) / 128) * ((d.k + BK - 1) / BK);
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(total, di.sm_count)));
+    // per CTA one parked partial (BT x 128 accumulators) and one flag
+    const size_t ws_bytes = static_cast<size_t>(grid) * BT * 128 * 4;
+    const size_t fl_bytes = static_cast<size_t>(grid) * 4;
+    void* ws = nullptr;
+    st = scratch_alloc(&ws, ws_bytes + fl_bytes, s);
+    if (st != NQ_SUCCESS) return st;
+    uint32_t* flags = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ws_bytes);
+    cudaError_t e = cudaMemsetAsync(flags, 0, fl_bytes, s);
+    if (e == cudaSuccess) {
+        kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(mw, mx, d.m, d.n, d.k, idesc, ep, static_cast<uint32_t*>(ws), flags,
+                                                    device_error_word());
+        e = cudaGetLastError();
+    }
+    scratch_free(ws, s);
+    return cuda_status(e, "nq_gemm (decode)");
+}
+
+template <bool I8, bool KN>
+nq_status_t launch_decode(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
+                          const DeviceInfo& di) {
+    if (d.m <= 16) return launch_decode_bt<I8, KN, 16>(d, a, b, ep, s, di);
+    return launch_decode_bt<I8, KN, 32>(d, a, b, ep, s, di);
+}
+
+// Few tokens against a large weight: too few output tiles to fill the SMs.
+// Measured on B200 (K=8192, N=28672): the swapped stream-K path streams the
+// weights faster up to 32 tokens; from 64 tokens on, re-reading the token
+// tile for every weight slice costs more than it saves.
+bool use_decode(const nq_gemm_desc_t& d, int sm_count) {
+    if (d.m > 32) return false;
+    const long long tiles = static_cast<long long>((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
+    return tiles < 2LL * sm_count && static_cast<long long>(d.n) * d.k >= (16LL << 20);
+}
+
 template <bool I8, bool KN>
 nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                       const DeviceInfo& di) {
+    if (use_decode(d, di.sm_count)) return launch_decode<I8, KN>(d, a, b, ep, s, di);
     if (d.m > BM) {
         if (d.out_dtype == NQ_BF16) return launch_tc2<I8, KN, 1>(d, a, b, ep.out, ep, s, di);
         if (d.out_dtype == NQ_S8) return launch_tc2<I8, KN, 2>(d, a, b, ep.out, ep, s, di);

@@ -243,3 +243,51 @@ def test_tail_split_fp8_vs_torch(nq, m, n, k):
     err = ((out.double() - ref).abs() / torch.maximum(ref.abs(), 1e-2 * ref.pow(2).mean().sqrt())).max()
     assert float(err) <= FP8_TOL_F32_OBSERVED
     assert nq.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("m", [1, 16, 17, 32, 40, 64, 200, 256])
+@pytest.mark.parametrize("b_layout", [1, 0])
+def test_decode_int8_exact_vs_oracle(nq, m, b_layout):
+    """Decode-shaped INT8 (BASELINE configs[3] pattern at reduced N/K): the
+    swap-AB stream-K path with int32 red.add partials must be exact, and the
+    scaled bf16 output bit-identical to the oracle epilogue."""
+    import oracle_lib as O
+    n, k = 4096, 4096
+    a = int8_operand((m, k), m)
+    b = int8_operand((k, n) if b_layout == 0 else (n, k), 99)
+    acc = O.gemm_i8_acc(a, b, b_layout == 0)
+    np.testing.assert_array_equal(run_gemm(nq, a, b, m, n, k, 2, 2, b_layout, 2), acc)
+    rs = (np.random.default_rng(1).random(m) * 0.01 + 1e-3).astype(np.float32)
+    cs = (np.random.default_rng(2).random(n) * 0.01 + 1e-3).astype(np.float32)
+    got = run_gemm(nq, a, b, m, n, k, 2, 2, b_layout, 1, 1.0, rs, cs)
+    np.testing.assert_array_equal(got, O.epilogue(acc, True, 1.0, rs, cs))
+
+
+@pytest.mark.parametrize("m", [16, 32, 256])
+def test_decode_fp8_vs_oracle(nq, m):
+    import oracle_lib as O
+    n, k = 4096, 4096
+    a, sa = fp8_operand((m, k), 3, 0)
+    b, sb = fp8_operand((n, k), 4, 0)
+    alpha = float(np.float32(sa) * np.float32(sb))
+    got = run_gemm(nq, a, b, m, n, k, 0, 0, 1, 0, alpha)
+    ref = O.epilogue(O.gemm_fp8_acc(a, b, 0, 0, False), False, alpha)
+    assert rel_err(got, ref) <= FP8_TOL_F32_OBSERVED
+
+
+def test_decode_config3_full_size_vs_torch(nq):
+    """BASELINE configs[3] at full size (K=8192, N=28672) for M=16: exact int32
+    against torch._int_mm."""
+    import torch
+    from gpu_util import stream
+    m, k, n = 16, 8192, 28672
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+    w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+    out = torch.empty(m, n, dtype=torch.int32, device="cuda")
+    nq.gemm(nq.make_desc(m, n, k, 2, 2, 1, 2, 1.0), x.data_ptr(), w.data_ptr(), out.data_ptr(), stream())
+    xm = torch.zeros(32, k, dtype=torch.int8, device="cuda")
+    xm[:m] = x
+    ref = torch._int_mm(xm, w.t().contiguous())[:m]
+    assert torch.equal(out, ref)
+    assert nq.device_error_flags() == 0
