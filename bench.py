@@ -10,6 +10,9 @@ reference's K x N layout (FP8GEMM::forward).  One step = one GEMM launch.
 
 N > 1 (torchrun): every rank runs the same GEMM on its own GPU (replicas, no
 collective on the data path); value = all ranks' FLOPs / max-over-ranks time.
+The "tp_mlp" block times BASELINE configs[4], the tensor-parallel FP8 SwiGLU
+MLP, with tp = N (strong scaling, T = 16384 tokens at every N, bf16 NCCL
+all-reduce of the row-parallel output).
 --impl reference times the reference algorithm on the host cores (the CPU
 oracle port of FP8GEMM::forward's naive kernel, fp8_gemm.cu:64-86), rank 0 only.
 """
@@ -281,6 +284,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
     e2e_value = world * FLOPS / (e2e_ms * 1e-3) / 1e12
+    del da, db, flush
+    torch.cuda.empty_cache()
+    tp_res = None
+    if not args.no_tp_mlp:
+        tp_res = tp_mlp_bench(world, rank, max(3, min(args.steps, 10)), args.warmup if args.warmup < 5 else 5,
+                              chunks=args.tp_chunks, overlap=args.tp_overlap)
 
     if rank != 0:
         if world > 1:
@@ -306,13 +315,19 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
+    if tp_res is not None:
+        line["tp_mlp"] = tp_res
     if args.cublas:
-        line["library_comparison"] = cublaslt_fp8(args.steps, args.warmup, flush)
+        line["library_comparison"] = cublaslt_fp8(args.steps, args.warmup,
+                                                  torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda"))
     if not args.no_secondary:
         line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"])}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
     return 0
 
 
@@ -363,6 +378,54 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20)):
     return out
 
 
+def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4, overlap="full"):
+    """the FP8 SwiGLU MLP (nova_b200.tp.TensorParallelMLP)
+    with tp = world size, T tokens per step (strong scaling: the same T at
+    every tp).  x ~ N(0,1) bf16, weights ~ N(0,0.02) fp32 generated on the
+    device from fixed seeds (identical on every rank), sharded and FP8
+    quantized by set_weight.  One step = forward() (per-token quantize,
+    gate/up GEMM + SwiGLU, quantize, down GEMM, chunked bf16 NCCL
+    all-reduce); time = max over ranks of the CUDA-event time of `steps`
+    forwards.  Inputs (256 MiB) and weights exceed L2."""
+    import torch
+    from nova_b200.tp import TensorParallelMLP
+    g = torch.Generator(device="cuda").manual_seed(11)
+    mlp = TensorParallelMLP(H, I, chunks=chunks, overlap=overlap)
+    wg = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
+    wu = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
+    wd = torch.randn(I, H, device="cuda", generator=g).mul_(0.02)
+    mlp.set_weight(wg, wu, wd)
+    del wg, wu, wd
+    torch.cuda.empty_cache()
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    for _ in range(warmup):
+        mlp.forward(x, out, 1, T, sync=False)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        mlp.forward(x, out, 1, T, sync=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    flops = 6.0 * T * H * I
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    tflops = flops / (ms * 1e-3) / 1e12
+    res = {"workload": "tp_fp8_swiglu_mlp (BASELINE configs[4])", "tokens": T, "hidden": H, "intermediate": I,
+           "tp": world, "chunks": chunks, "overlap": overlap, "ms_per_step": round(ms, 4),
+           "tokens_per_s": T / (ms * 1e-3), "tflops_total": tflops,
+           "frac_of_tp_x_fp8_peak": tflops / (world * fp8_peak),
+           "allreduce_bytes": 2 * T * H if world > 1 else 0, "scaling": "strong"}
+    del mlp, x, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def cublaslt_fp8(steps, warmup, flush):
     """cuBLASLt FP8 (torch._scaled_mm, e4m3 x e4m3 -> bf16, per-tensor scales)
     on the same shape, timed the same way: the library number to beat, and at
@@ -400,6 +463,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cublas", action="store_true", help="also time cuBLASLt FP8 on the same shape")
     ap.add_argument("--no-secondary", action="store_true", help="skip the quantize bandwidth sweep")
+    ap.add_argument("--no-tp-mlp", action="store_true", help="skip the TP SwiGLU MLP (configs[4]) block")
+    ap.add_argument("--tp-chunks", type=int, default=4)
+    ap.add_argument("--tp-overlap", choices=["full", "down"], default="full")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -181,6 +181,16 @@ nq_status_t nq_quantize_cols_noalloc(const float* src, uint8_t* dst, float* scal
  *   int32 accumulators, INT8 only).
  * Shapes with K % 16, N % 16 or pointers not 16-byte aligned run a SIMT
  * kernel with the same arithmetic. */
+/* Epilogue functions applied after the scales:
+   NQ_EPI_SWIGLU: the N columns of B hold gate and up weights packed in
+   alternating 128-column blocks ([g_0 | u_0 | g_1 | u_1 | ...], block j of
+   the output = columns 256j..256j+255 of B); the output is M x N/2 with
+   out[:, 128j + c] = silu(g) * u, silu(g) = g / (1 + exp(-g)), g and u the
+   scaled values of packed columns 256j + c and 256j + 128 + c (the fused form
+   of silu_and_mul, activations.cu:80-92).  Needs N % 256 == 0 and the
+   tensor-core path; col_scale and bias are indexed by packed column. */
+typedef enum { NQ_EPI_NONE = 0, NQ_EPI_SWIGLU = 1 } nq_epilogue_t;
+
 typedef struct {
     int m, n, k;
     nq_format_t a_format, b_format;
@@ -190,6 +200,7 @@ typedef struct {
     const float* row_scale; /* [m] device, or NULL */
     const float* col_scale; /* [n] device, or NULL */
     const float* bias;      /* [n] device, or NULL */
+    nq_epilogue_t epilogue; /* NQ_EPI_NONE unless stated */
 } nq_gemm_desc_t;
 
 nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out,

@@ -34,7 +34,7 @@ class NqError(RuntimeError):
 class GemmDesc(C.Structure):
     _fields_ = [("m", C.c_int), ("n", C.c_int), ("k", C.c_int), ("a_format", C.c_int), ("b_format", C.c_int),
                 ("b_layout", C.c_int), ("out_dtype", C.c_int), ("alpha", C.c_float), ("row_scale", C.c_void_p),
-                ("col_scale", C.c_void_p), ("bias", C.c_void_p)]
+                ("col_scale", C.c_void_p), ("bias", C.c_void_p), ("epilogue", C.c_int)]
 
 
 _SIGS = {
@@ -101,10 +101,13 @@ def exported_symbols():
     return sorted(list(_SIGS) + ["nq_status_string", "nq_last_error", "nq_version", "nq_fp8_gemm_workspace_size"])
 
 
+EPI_NONE, EPI_SWIGLU = 0, 1
+
+
 def make_desc(m, n, k, a_format=E4M3, b_format=E4M3, b_layout=B_KN, out_dtype=BF16, alpha=1.0,
-              row_scale=0, col_scale=0, bias=0) -> GemmDesc:
+              row_scale=0, col_scale=0, bias=0, epilogue=EPI_NONE) -> GemmDesc:
     return GemmDesc(m, n, k, a_format, b_format, b_layout, out_dtype, alpha, row_scale or None,
-                    col_scale or None, bias or None)
+                    col_scale or None, bias or None, epilogue)
 
 
 def device_error_flags(clear: bool = True) -> int:

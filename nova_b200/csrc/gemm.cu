@@ -375,7 +375,9 @@ constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_B
 
 // OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
 // 1 = bf16 through TMA stores, 2 = int8 requantized, direct stores.
-template <bool INT8_KIND, bool B_KN, int OUTK>
+// SWIGLU: columns [0,128) of each 256-wide tile are gate, [128,256) up; the
+// tile writes 128 columns of silu(g) * u.
+template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
@@ -549,6 +551,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             }
             const int row0_warp = mb * P_BM + static_cast<int>(rank) * 128 + quarter * 32;
             const float rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+            if constexpr (SWIGLU) {
+                // this warp's 64 output columns: gate TMEM columns colh*64 + [0,64),
+                // up columns 128 + colh*64 + [0,64)
+                const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
+#pragma unroll 1
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t g[32], u[32];
+                    tmem_ld_32x32b_x32(tbase + colh * 64 + c * 32, g);
+                    tmem_ld_32x32b_x32(tbase + 128 + colh * 64 + c * 32, u);
+                    tmem_ld_wait();
+                    if (c == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (rank == 0) mbar_arrive(&tempty[acc]);
+                            else mbar_arrive_remote(tempty_leader + 8u * acc);
+                        }
+                    }
+                    const int gcol0 = nb * P_BN + colh * 64 + c * 32;
+                    const int hcol0 = nb * (P_BN / 2) + colh * 64 + c * 32;
+                    if (row0_warp >= M) continue;
+                    const ColOps gop = col_ops(ep.col_scale, ep.bias, gcol0, lane, N);
+                    const ColOps uop = col_ops(ep.col_scale, ep.bias, gcol0 + 128, lane, N);
+                    uint8_t* slot = slots + (chunk_seq & 1) * P_EPI_SLOT;
+                    if (lane == 0) bulk_wait_group_read<1>();
+                    __syncwarp();
+                    float h[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float gv = epi_elem(__uint_as_float(g[j]), ep.alpha, rs, gop, j);
+                        const float uv = epi_elem(__uint_as_float(u[j]), ep.alpha, rs, uop, j);
+                        h[j] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                    }
+                    if (OUTK == 1) {
+                        uint8_t* rowp = slot + lane * 64;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint4 q;
+                            q.x = f32x2_to_bf16x2(h[8 * j], h[8 * j + 1]);
+                            q.y = f32x2_to_bf16x2(h[8 * j + 2], h[8 * j + 3]);
+                            q.z = f32x2_to_bf16x2(h[8 * j + 4], h[8 * j + 5]);
+                            q.w = f32x2_to_bf16x2(h[8 * j + 6], h[8 * j + 7]);
+                            *reinterpret_cast<uint4*>(rowp + 16 * (j ^ ((lane >> 1) & 3))) = q;
+                        }
+                    } else {
+                        uint8_t* rowp = slot + lane * 128;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            *reinterpret_cast<uint4*>(rowp + 16 * (j ^ (lane & 7))) =
+                                make_uint4(__float_as_uint(h[4 * j]), __float_as_uint(h[4 * j + 1]),
+                                           __float_as_uint(h[4 * j + 2]), __float_as_uint(h[4 * j + 3]));
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, slot, hcol0, row0_warp);
+                        bulk_commit_group();
+                    }
+                    ++chunk_seq;
+                }
+                continue;
+            }
             // this warp's 128 columns, 32 per tcgen05.ld, the next 32 in flight
             uint32_t r[32];
             uint4 w[8];
@@ -1003,7 +1067,7 @@ nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
     return NQ_SUCCESS;
 }
 
-template <bool I8, bool KN, int OUTK>
+template <bool I8, bool KN, int OUTK, bool SWIGLU = false>
 nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, void* out, const Epi& ep,
                        cudaStream_t s, const DeviceInfo& di) {
     CUtensorMap ma, mb, mc;
@@ -1012,11 +1076,16 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     if (KN) st = make_map(&mb, b, d.n, d.k, d.n, 128, BK);
     else st = make_map(&mb, b, d.k, d.n, d.k, BK, 128);
     if (st != NQ_SUCCESS) return st;
-    if (d.out_dtype != NQ_S8) st = make_out_map(&mc, out, d);
-    else std::memset(&mc, 0, sizeof(mc));
+    if (d.out_dtype != NQ_S8) {
+        nq_gemm_desc_t od = d;
+        if (SWIGLU) od.n = d.n / 2;
+        st = make_out_map(&mc, out, od);
+    } else {
+        std::memset(&mc, 0, sizeof(mc));
+    }
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
-    auto kern = k_gemm_tc2<I8, KN, OUTK>;
+    auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU>;
     static uint64_t attr_set = 0;
     st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
@@ -1043,7 +1112,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     const int rem = tiles % clusters;
     // Splitting pays off only when a tile's MMA time clearly exceeds its
     // epilogue (part 0's epilogue waits for part 1's): long K only.
-    const int split = (rem && clusters / rem >= 2 && kblocks >= 48) ? 2 : 1;
+    const int split = (!SWIGLU && rem && clusters / rem >= 2 && kblocks >= 48) ? 2 : 1;
     void* scratch = nullptr;
     if (split >= 2) {
         tail.full_units = tiles - rem;
@@ -1123,6 +1192,11 @@ bool use_decode(const nq_gemm_desc_t& d, int sm_count) {
 template <bool I8, bool KN>
 nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                       const DeviceInfo& di) {
+    if (d.epilogue == NQ_EPI_SWIGLU) {
+        if (I8) return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm: SwiGLU epilogue is FP8-only");
+        if (d.out_dtype == NQ_BF16) return launch_tc2<I8, KN, 1, true>(d, a, b, ep.out, ep, s, di);
+        return launch_tc2<I8, KN, 0, true>(d, a, b, ep.out, ep, s, di);
+    }
     if (use_decode(d, di.sm_count)) return launch_decode<I8, KN>(d, a, b, ep, s, di);
     if (d.m > BM) {
         if (d.out_dtype == NQ_BF16) return launch_tc2<I8, KN, 1>(d, a, b, ep.out, ep, s, di);
@@ -1182,13 +1256,19 @@ nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, voi
     if (d->b_layout != NQ_B_KN && d->b_layout != NQ_B_NK) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: b_layout");
     if (d->out_dtype != NQ_F32 && d->out_dtype != NQ_BF16 && d->out_dtype != NQ_S8 && !(i8 && d->out_dtype == NQ_S32))
         return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: out_dtype");
+    if (d->epilogue != NQ_EPI_NONE && d->epilogue != NQ_EPI_SWIGLU)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm: epilogue");
+    const bool swiglu = d->epilogue == NQ_EPI_SWIGLU;
+    if (swiglu && (d->n % 256 != 0 || i8 || (d->out_dtype != NQ_BF16 && d->out_dtype != NQ_F32)))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm: SwiGLU needs FP8 operands, N % 256 == 0 and f32/bf16 output");
     DeviceInfo di;
     nq_status_t st = current_device(&di);
     if (st != NQ_SUCCESS) return st;
-    Epi ep{out, d->n, d->out_dtype, d->alpha, d->row_scale, d->col_scale, d->bias};
+    Epi ep{out, swiglu ? d->n / 2 : d->n, d->out_dtype, d->alpha, d->row_scale, d->col_scale, d->bias};
     const bool kn = d->b_layout == NQ_B_KN;
     const bool tc_ok = !force_simt && d->k > 0 && d->k % 16 == 0 && d->n % 16 == 0 && aligned16(a) && aligned16(b) &&
                        aligned16(out);
+    if (swiglu && !tc_ok) return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm: SwiGLU needs the tensor-core path (aligned operands)");
     if (tc_ok) {
         if (i8) return kn ? launch_tc<true, true>(*d, a, b, ep, s, di) : launch_tc<true, false>(*d, a, b, ep, s, di);
         return kn ? launch_tc<false, true>(*d, a, b, ep, s, di) : launch_tc<false, false>(*d, a, b, ep, s, di);
@@ -1225,6 +1305,7 @@ static nq_status_t fp8_forward(const uint8_t* a, const uint8_t* b, float* out, i
     d.b_layout = NQ_B_KN;
     d.out_dtype = NQ_F32;
     d.alpha = (sa * sb) * so;
+    d.epilogue = NQ_EPI_NONE;
     return nq::gemm_impl(&d, a, b, out, s, 0);
 }
 

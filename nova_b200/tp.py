@@ -1,0 +1,298 @@
+"""Tensor-parallel quantized layers and the SwiGLU MLP.
+
+Mirror of pplmx/nova's cuda::neural tensor-parallel layers
+(include/cuda/neural/tensor_parallel_layers.h:51 ColumnParallelLayer, :194
+RowParallelLayer, :328 TensorParallelMLP; forward of the MLP at
+src/cuda/neural/tensor_parallel_layers.cpp:561-579): gate and up are
+column-parallel, down is row-parallel, one all-reduce sums the row-parallel
+output.  Here the layers are W8A8 FP8 on the tcgen05 GEMMs of libnova_q:
+
+  x (bf16, replicated)   -> per-token FP8 quantize          nq_quantize_rows
+  [Wg|Wu] column shards  -> one GEMM, fused silu(g)*u       nq_gemm + NQ_EPI_SWIGLU
+  h (bf16, this shard)   -> per-token FP8 quantize          nq_quantize_rows
+  Wd row shard           -> partial output (bf16)           nq_gemm
+  partial                -> sum over ranks (bf16 NCCL all-reduce through
+                            torch.distributed, chunked along the tokens so
+                            the down-projection of chunk i+1 overlaps the
+                            all-reduce of chunk i)
+
+Weights are per-output-channel FP8 E4M3 (scale = column amax / 448, computed
+on each rank's shard).  Shard layouts follow the reference set_weight
+(column shard: columns [r*N/tp, (r+1)*N/tp) of a row-major K x N weight,
+tensor_parallel_layers.cpp:111-136; row shard: rows [r*K/tp, ...), :344-368).
+The reference takes an NcclContext; these classes take a torch.distributed
+process group (NCCL on GPUs), whose size is the TP degree.  Streams, device
+memory and the collective come from PyTorch; all arithmetic runs in libnova_q.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+BLOCK = 128  # gate/up packing granularity of the SwiGLU epilogue
+
+
+# ---- pure host logic (tested on CPU) ------------------------------------------
+def shard_columns(w, rank: int, tp: int):
+    """Column shard of a row-major K x N weight (tensor_parallel_layers.cpp:111-136)."""
+    n = w.shape[1]
+    if n % tp:
+        raise ValueError(f"out_features {n} is not divisible by tp={tp}")
+    nl = n // tp
+    return w[:, rank * nl:(rank + 1) * nl]
+
+
+def shard_rows(w, rank: int, tp: int):
+    """Row shard of a row-major K x N weight (tensor_parallel_layers.cpp:344-368)."""
+    k = w.shape[0]
+    if k % tp:
+        raise ValueError(f"in_features {k} is not divisible by tp={tp}")
+    kl = k // tp
+    return w[rank * kl:(rank + 1) * kl]
+
+
+def swiglu_pack_order(n_local: int) -> np.ndarray:
+    """Column order of the packed [gate | up] weight: block j of 256 columns is
+    gate columns 128j..128j+127 followed by up columns 128j..128j+127, indexed
+    into the concatenation [gate (n_local) | up (n_local)]."""
+    if n_local % BLOCK:
+        raise ValueError(f"intermediate shard {n_local} must be a multiple of {BLOCK}")
+    j = np.arange(n_local // BLOCK)[:, None]
+    c = np.arange(BLOCK)[None, :]
+    return np.concatenate([j * BLOCK + c, n_local + j * BLOCK + c], axis=1).reshape(-1)
+
+
+def chunk_bounds(tokens: int, chunks: int, align: int = 256):
+    """Token ranges of the overlapped GEMM / all-reduce pipeline, each a
+    multiple of `align` rows except the last."""
+    if tokens <= 0:
+        return []
+    chunks = max(1, min(chunks, (tokens + align - 1) // align))
+    step = ((tokens + chunks - 1) // chunks + align - 1) // align * align
+    return [(r0, min(tokens, r0 + step)) for r0 in range(0, tokens, step)]
+
+
+def reduce_pipeline(bounds, compute, group=None, tp: int = 1):
+    """For each token range: compute(r0, r1) enqueues the partial rows and
+    returns the tensor view holding them; with tp > 1 an asynchronous sum
+    all-reduce of that view follows at once, so the next range's GEMM runs
+    while this one is on the wire (RowParallelLayer::forward's all_reduce,
+    tensor_parallel_layers.cpp:406, split into chunks).  Waits for every
+    all-reduce before returning."""
+    import torch.distributed as dist
+    works = []
+    for r0, r1 in bounds:
+        view = compute(r0, r1)
+        if tp > 1:
+            works.append(dist.all_reduce(view, op=dist.ReduceOp.SUM, group=group, async_op=True))
+    for w in works:
+        w.wait()
+
+
+def _group_info(group):
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+def _as_tensor(w):
+    import torch
+    return w if isinstance(w, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(w, np.float32))
+
+
+# ---- layers ------------------------------------------------------------------------
+class _FP8Linear:
+    """Per-channel FP8 E4M3 weight (K x N, row-major) on the current device,
+    applied to per-token FP8 activations with a bf16 output."""
+
+    def __init__(self):
+        import torch
+        from . import capi
+        self.nq, self.torch = capi, torch
+        self.q = self.s = None
+        self._ws = {}
+
+    def load(self, w):
+        t, nq = self.torch, self.nq
+        dev = t.device("cuda", t.cuda.current_device())
+        w = w.to(dev, t.float32).contiguous()
+        k, n = w.shape
+        self.k, self.n = k, n
+        self.q = t.empty(k, n, dtype=t.uint8, device=dev)
+        self.s = t.empty(n, dtype=t.float32, device=dev)
+        nq.quantize_cols(w.data_ptr(), self.q.data_ptr(), self.s.data_ptr(), k, n, nq.E4M3,
+                         t.cuda.current_stream().cuda_stream)
+
+    def act(self, x, T, r0=0, r1=None):
+        """Per-token FP8 quantize of rows [r0, r1) of a bf16 T x K activation
+        into this layer's T-row code/scale buffers -> (codes, scales)."""
+        t, nq = self.torch, self.nq
+        r1 = T if r1 is None else r1
+        if T not in self._ws:
+            self._ws = {T: (t.empty(T, self.k, dtype=t.uint8, device=x.device),
+                            t.empty(T, dtype=t.float32, device=x.device))}
+        xq, sx = self._ws[T]
+        if r1 > r0:
+            nq.quantize_rows(x.data_ptr() + 2 * r0 * self.k, nq.BF16, xq.data_ptr() + r0 * self.k,
+                             sx.data_ptr() + 4 * r0, r1 - r0, self.k, nq.E4M3, t.cuda.current_stream().cuda_stream)
+        return xq, sx
+
+    def gemm(self, xq, sx, out, r0, r1, epilogue=0):
+        nq = self.nq
+        n_out = self.n // 2 if epilogue else self.n
+        d = nq.make_desc(r1 - r0, self.n, self.k, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0,
+                         sx.data_ptr() + 4 * r0, self.s.data_ptr(), 0, epilogue)
+        nq.gemm(d, xq.data_ptr() + r0 * self.k, self.q.data_ptr(), out.data_ptr() + 2 * r0 * n_out,
+                self.torch.cuda.current_stream().cuda_stream)
+
+
+def _check_io(t, x, T, cols, name):
+    if x.dtype != t.bfloat16 or not x.is_cuda or not x.is_contiguous() or x.numel() != T * cols:
+        raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor of {T} x {cols}")
+
+
+class ColumnParallelLayer:
+    """W8A8 FP8 column-parallel linear (tensor_parallel_layers.h:51): input
+    [batch*seq x in_features] replicated, output [batch*seq x out_features/tp]
+    this rank's column block, no communication."""
+
+    def __init__(self, in_features: int, out_features: int, group=None):
+        import torch
+        self.torch, self.group = torch, group
+        self.rank, self.tp = _group_info(group)
+        if out_features % self.tp:
+            raise ValueError("out_features must be divisible by the TP degree")
+        self.in_features, self.out_features = in_features, out_features
+        self.lin = _FP8Linear()
+
+    def set_weight(self, weight):
+        """Full weight [in_features x out_features], row-major (host or device)."""
+        self.lin.load(shard_columns(_as_tensor(weight), self.rank, self.tp))
+        self.torch.cuda.current_stream().synchronize()
+
+    def forward(self, input, output, batch: int, seq: int):
+        T = batch * seq
+        if self.lin.q is None:
+            raise RuntimeError("ColumnParallelLayer: set_weight has not been called")
+        _check_io(self.torch, input, T, self.in_features, "input")
+        _check_io(self.torch, output, T, self.out_features // self.tp, "output")
+        if T == 0:
+            return output
+        xq, sx = self.lin.act(input, T)
+        self.lin.gemm(xq, sx, output, 0, T)
+        self.torch.cuda.current_stream().synchronize()
+        return output
+
+
+class RowParallelLayer:
+    """W8A8 FP8 row-parallel linear (tensor_parallel_layers.h:194): input
+    [batch*seq x in_features/tp] this rank's shard, output [batch*seq x
+    out_features] replicated after the sum all-reduce (bf16, chunked)."""
+
+    def __init__(self, in_features: int, out_features: int, group=None, chunks: int = 4):
+        import torch
+        self.torch, self.group, self.chunks = torch, group, chunks
+        self.rank, self.tp = _group_info(group)
+        if in_features % self.tp:
+            raise ValueError("in_features must be divisible by the TP degree")
+        self.in_features, self.out_features = in_features, out_features
+        self.lin = _FP8Linear()
+
+    def set_weight(self, weight):
+        self.lin.load(shard_rows(_as_tensor(weight), self.rank, self.tp))
+        self.torch.cuda.current_stream().synchronize()
+
+    def forward(self, input, output, batch: int, seq: int, sync: bool = True):
+        T = batch * seq
+        if self.lin.q is None:
+            raise RuntimeError("RowParallelLayer: set_weight has not been called")
+        _check_io(self.torch, input, T, self.in_features // self.tp, "input")
+        _check_io(self.torch, output, T, self.out_features, "output")
+        if T == 0:
+            return output
+        xq, sx = self.lin.act(input, T)
+
+        def compute(r0, r1):
+            self.lin.gemm(xq, sx, output, r0, r1)
+            return output[r0:r1]
+
+        reduce_pipeline(chunk_bounds(T, self.chunks if self.tp > 1 else 1), compute, self.group, self.tp)
+        if sync:
+            self.torch.cuda.current_stream().synchronize()
+        return output
+
+
+class TensorParallelMLP:
+    """out = down( silu(gate(x)) * up(x) ) (tensor_parallel_layers.h:328).
+    hidden_dim H, intermediate_size I, tp = size of `group`.  set_weight
+    takes the FULL fp32 weights in the reference layout (gate, up: H x I;
+    down: I x H, row-major); forward(input, output, batch, seq) reads and
+    writes bf16 device tensors of [batch*seq x H] and synchronises the
+    stream, as the reference's forward does.  Gate and up of this rank's
+    shard are one packed FP8 weight (alternating 128-column blocks) so one
+    GEMM with the SwiGLU epilogue produces silu(g) * u directly."""
+
+    def __init__(self, hidden_dim: int, intermediate_size: int, group=None, chunks: int = 4,
+                 overlap: str = "full"):
+        import torch
+        if overlap not in ("full", "down"):
+            raise ValueError("overlap must be 'full' or 'down'")
+        self.torch, self.group, self.overlap = torch, group, overlap
+        self.rank, self.tp = _group_info(group)
+        if intermediate_size % (self.tp * BLOCK):
+            raise ValueError("intermediate_size must be a multiple of 128 * tp")
+        if hidden_dim % 16:
+            raise ValueError("hidden_dim must be a multiple of 16")
+        self.H, self.I = hidden_dim, intermediate_size
+        self.I_local = intermediate_size // self.tp
+        self.chunks = chunks
+        self.gate_up = _FP8Linear()
+        self.down = RowParallelLayer(intermediate_size, hidden_dim, group, chunks)
+        self._h = {}
+
+    def set_weight(self, gate_weight, up_weight, down_weight):
+        """Full weights (host or device, fp32): keeps this rank's shards."""
+        t = self.torch
+        dev = t.device("cuda", t.cuda.current_device())
+        g = shard_columns(_as_tensor(gate_weight), self.rank, self.tp).to(dev, t.float32)
+        u = shard_columns(_as_tensor(up_weight), self.rank, self.tp).to(dev, t.float32)
+        order = t.from_numpy(swiglu_pack_order(self.I_local))
+        # per-column scales do not depend on the column order, so quantizing
+        # the packed matrix equals packing the separately quantized shards
+        self.gate_up.load(t.cat([g, u], dim=1).index_select(1, order.to(g.device)))
+        self.down.set_weight(down_weight)
+
+    def forward(self, input, output, batch: int, seq: int, sync: bool = True):
+        """overlap = "full": the token chunks run the whole MLP (gate/up GEMM,
+        quantize, down GEMM) back to back, so chunk i's all-reduce overlaps
+        chunk i+1's three kernels; "down": gate/up for all tokens first, then
+        only the down-projection is chunked."""
+        t = self.torch
+        T = batch * seq
+        if self.gate_up.q is None:
+            raise RuntimeError("TensorParallelMLP: set_weight has not been called")
+        _check_io(t, input, T, self.H, "input")
+        _check_io(t, output, T, self.H, "output")
+        if T == 0:
+            return output
+        if T not in self._h:
+            self._h = {T: t.empty(T, self.I_local, dtype=t.bfloat16, device=input.device)}
+        h = self._h[T]
+        epi = self.gate_up.nq.EPI_SWIGLU
+        down = self.down.lin
+        xq, sx = self.gate_up.act(input, T)
+        bounds = chunk_bounds(T, self.chunks if self.tp > 1 else 1)
+        if self.overlap == "down" or len(bounds) == 1:
+            self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)
+
+        def compute(r0, r1):
+            if self.overlap != "down" and len(bounds) > 1:
+                self.gate_up.gemm(xq, sx, h, r0, r1, epilogue=epi)
+            hq, sh = down.act(h, T, r0, r1)
+            down.gemm(hq, sh, output, r0, r1)
+            return output[r0:r1]
+
+        reduce_pipeline(bounds, compute, self.group, self.tp)
+        if sync:
+            t.cuda.current_stream().synchronize()
+        return output

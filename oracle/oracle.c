@@ -581,3 +581,19 @@ int orc_quantized_tensor_from_float(const float* data, size_t n, float scale, in
 
 /* silu_and_mul_kernel, src/cuda/neural/activations.cu:80-92: g/(1+exp(-g))*u */
 float orc_silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+void orc_swiglu_epilogue(const float* acc, void* out, int out_bf16, int m, int n, float alpha,
+                         const float* row_scale, const float* col_scale, const float* bias) {
+    const int no = n / 2;
+    for (int i = 0; i < m; ++i)
+        for (int j = 0; j < no; ++j) {
+            const int gc = (j / 128) * 256 + (j % 128), uc = gc + 128;
+            float g = acc[(size_t)i * n + gc] * alpha, u = acc[(size_t)i * n + uc] * alpha;
+            if (row_scale) { g = g * row_scale[i]; u = u * row_scale[i]; }
+            if (col_scale) { g = g * col_scale[gc]; u = u * col_scale[uc]; }
+            if (bias) { g = g + bias[gc]; u = u + bias[uc]; }
+            const float h = g / (1.0f + expf(-g)) * u;
+            if (out_bf16) ((uint16_t*)out)[(size_t)i * no + j] = orc_f32_to_bf16(h);
+            else ((float*)out)[(size_t)i * no + j] = h;
+        }
+}

@@ -109,6 +109,11 @@ int orc_quantized_tensor_from_float(const float* data, size_t n, float scale, in
 
 /* SwiGLU of the TP MLP (activations.cu:80-92 restated on fp32 values) */
 float orc_silu_mul(float g, float u);
+/* Fused SwiGLU GEMM epilogue: acc is m x n fp32 with gate/up packed in
+   alternating 128-column blocks; out (m x n/2, fp32 or bf16 bits) holds
+   silu(g) * u of the scaled values (orc_epilogue's arithmetic for g and u). */
+void orc_swiglu_epilogue(const float* acc, void* out, int out_bf16, int m, int n, float alpha,
+                         const float* row_scale, const float* col_scale, const float* bias);
 
 /* bounded multi-threaded run of orc_fp8_gemm_reference over rows
    [row0, row0+rows); returns the number of threads used */

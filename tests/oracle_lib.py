@@ -46,6 +46,8 @@ for name, res, args in [
     ("orc_quantized_matmul", None, [_p, _p, _p, _i, _i, _i, _f, _f]),
     ("orc_quantized_tensor_from_float", _i, [_p, _sz, _f, _p, _p]),
     ("orc_fp8_gemm_reference_rows_mt", _i, [_p, _p, _p, _i, _i, _i, _f, _f, _f, _i, _i, _i]),
+    ("orc_swiglu_epilogue", None, [_p, _p, _i, _i, _i, _f, _p, _p, _p]),
+    ("orc_silu_mul", _f, [_f, _f]),
 ]:
     fn = getattr(lib, name)
     fn.restype = res
@@ -247,3 +249,41 @@ def special_floats():
             grid.append((1.0 + (m + 0.5) / 16.0) * 2.0 ** e)
     v = np.array(base + grid, np.float32)
     return np.concatenate([v, -v])
+
+
+def swiglu_epilogue(acc, out_bf16, alpha, row_scale=None, col_scale=None, bias=None):
+    m, n = acc.shape
+    acc = np.ascontiguousarray(acc, np.float32)
+    out = np.empty((m, n // 2), np.uint16 if out_bf16 else np.float32)
+    rs = np.ascontiguousarray(row_scale, np.float32) if row_scale is not None else None
+    cs = np.ascontiguousarray(col_scale, np.float32) if col_scale is not None else None
+    bs = np.ascontiguousarray(bias, np.float32) if bias is not None else None
+    lib.orc_swiglu_epilogue(ptr(acc), ptr(out), int(out_bf16), m, n, alpha, ptr(rs) if rs is not None else None,
+                            ptr(cs) if cs is not None else None, ptr(bs) if bs is not None else None)
+    return out
+
+
+def tp_mlp_partial(x_bits, wg, wu, wd, rank, tp):
+    """One rank's row-parallel partial of the W8A8 FP8 SwiGLU MLP, restated on
+    the oracle: per-token E4M3 quantize of x (bf16 bits, T x H); gate/up
+    column shards (tensor_parallel_layers.cpp:111-136) with per-column E4M3
+    scales, packed in alternating 128-column blocks; the GEMM accumulators
+    and the SwiGLU epilogue (activations.cu:80-92) to bf16 h; per-token
+    quantize of h; the down row shard (:344-368) with per-column scales; bf16
+    partial.  Returns (h bits, partial bits)."""
+    T, H = x_bits.shape
+    I = wg.shape[1]
+    il = I // tp
+    xq, sx = quantize_rows(x_bits, 0, bf16=True)
+    g = wg[:, rank * il:(rank + 1) * il]
+    u = wu[:, rank * il:(rank + 1) * il]
+    j = np.arange(il // 128)[:, None]
+    c = np.arange(128)[None, :]
+    order = np.concatenate([j * 128 + c, il + j * 128 + c], axis=1).reshape(-1)
+    gu = np.ascontiguousarray(np.concatenate([g, u], axis=1)[:, order])
+    gq, gs = quantize_cols(gu, 0)
+    h = swiglu_epilogue(gemm_fp8_acc(xq, gq, 0, 0, True), True, 1.0, sx, gs)
+    hq, sh = quantize_rows(h, 0, bf16=True)
+    dq, ds = quantize_cols(np.ascontiguousarray(wd[rank * il:(rank + 1) * il]), 0)
+    part = epilogue(gemm_fp8_acc(hq, dq, 0, 0, True), True, 1.0, sh, ds)
+    return h, part

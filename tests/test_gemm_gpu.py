@@ -291,3 +291,46 @@ def test_decode_config3_full_size_vs_torch(nq):
     ref = torch._int_mm(xm, w.t().contiguous())[:m]
     assert torch.equal(out, ref)
     assert nq.device_error_flags() == 0
+
+
+def run_swiglu(nq, a, b, m, n, k, b_layout, out_dtype, alpha, row=None, col=None, bias=None):
+    from gpu_util import dev, empty, host, ptr, stream
+    d_a, d_b = dev(a), dev(b)
+    d_o = empty(m * (n // 2) * (4 if out_dtype == 0 else 2))
+    keep = [dev(v) if v is not None else None for v in (row, col, bias)]
+    desc = nq.make_desc(m, n, k, 0, 0, b_layout, out_dtype, alpha, *[ptr(t) if t is not None else 0 for t in keep],
+                        epilogue=nq.EPI_SWIGLU)
+    nq.gemm(desc, ptr(d_a), ptr(d_b), ptr(d_o), stream())
+    out = host(d_o, np.float32 if out_dtype == 0 else np.uint16, (m, n // 2))
+    assert nq.device_error_flags() == 0
+    return out
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 512, 256), (200, 1024, 512), (64, 256, 128), (384, 2048, 1024), (16, 768, 384)])
+@pytest.mark.parametrize("b_layout", [0, 1])
+def test_swiglu_epilogue_vs_oracle(nq, m, n, k, b_layout):
+    """Gate/up GEMM with the fused silu(g) * u epilogue (the TP MLP's first
+    layer): same accumulators as the plain GEMM, then the oracle's SwiGLU on
+    the scaled values; fp32 out within 1e-4, bf16 out within the FP8 bar."""
+    import oracle_lib as O
+    a, sa = fp8_operand((m, k), 30 + m, 0)
+    b, sb = fp8_operand((k, n) if b_layout == 0 else (n, k), 40 + n, 0)
+    rs = (np.random.default_rng(8).random(m) + 0.5).astype(np.float32) * np.float32(sa)
+    cs = (np.random.default_rng(9).random(n) + 0.5).astype(np.float32) * np.float32(sb)
+    bias = (np.random.default_rng(10).standard_normal(n) * 0.1).astype(np.float32)
+    acc = O.gemm_fp8_acc(a, b, 0, 0, b_layout == 0)
+    got32 = run_swiglu(nq, a, b, m, n, k, b_layout, 0, 1.0, rs, cs, bias)
+    ref32 = O.swiglu_epilogue(acc, False, 1.0, rs, cs, bias)
+    assert rel_err(got32, ref32) <= FP8_TOL_F32_OBSERVED
+    got16 = run_swiglu(nq, a, b, m, n, k, b_layout, 1, 1.0, rs, cs)
+    ref16 = O.swiglu_epilogue(acc, True, 1.0, rs, cs)
+    assert rel_err(O.bf16_bits_to_f32(got16), O.bf16_bits_to_f32(ref16)) <= FP8_TOL
+
+
+def test_swiglu_epilogue_rejects_unsupported(nq):
+    from gpu_util import empty, ptr, stream
+    buf = empty(1 << 20)
+    for n, fmt, od in [(384, 0, 1), (512, 2, 1), (512, 0, 3)]:
+        desc = nq.make_desc(128, n, 128, fmt, fmt, 0, od, 1.0, epilogue=nq.EPI_SWIGLU)
+        with pytest.raises(nq.NqError, match="UNSUPPORTED"):
+            nq.gemm(desc, ptr(buf), ptr(buf), ptr(buf), stream())

@@ -1,0 +1,120 @@
+"""Host logic of the tensor-parallel MLP, on CPU: weight sharding as the
+reference's set_weight slices it (tensor_parallel_layers.cpp:111-136,
+:344-368), the packed gate/up column order of the SwiGLU GEMM, the token
+chunking of the overlapped all-reduce, and the chunked all-reduce pipeline
+itself run by two gloo ranks on oracle-computed partials."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from nova_b200 import tp
+
+
+def test_shards_partition_the_weight():
+    w = np.arange(8 * 12, dtype=np.float32).reshape(8, 12)
+    for t in (1, 2, 4):
+        cols = [tp.shard_columns(w, r, t) for r in range(t)]
+        rows = [tp.shard_rows(w, r, t) for r in range(t)]
+        np.testing.assert_array_equal(np.concatenate(cols, axis=1), w)
+        np.testing.assert_array_equal(np.concatenate(rows, axis=0), w)
+        assert cols[-1].shape == (8, 12 // t) and rows[-1].shape == (8 // t, 12)
+    with pytest.raises(ValueError):
+        tp.shard_columns(w, 0, 5)
+    with pytest.raises(ValueError):
+        tp.shard_rows(w, 0, 3)
+
+
+def test_pack_order_is_block_interleaved_permutation():
+    for il in (128, 384, 3584):
+        o = tp.swiglu_pack_order(il)
+        assert sorted(o.tolist()) == list(range(2 * il))
+        blocks = o.reshape(-1, 256)
+        assert (blocks[:, :128] < il).all() and (blocks[:, 128:] >= il).all()
+        np.testing.assert_array_equal(blocks[:, 128:] - il, blocks[:, :128])
+    with pytest.raises(ValueError):
+        tp.swiglu_pack_order(200)
+
+
+@pytest.mark.parametrize("tokens,chunks", [(16384, 4), (300, 4), (256, 8), (1, 4), (1000, 1), (4097, 3)])
+def test_chunk_bounds_cover_tokens(tokens, chunks):
+    b = tp.chunk_bounds(tokens, chunks)
+    assert b[0][0] == 0 and b[-1][1] == tokens
+    assert all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+    assert all((r0 % 256) == 0 and r1 > r0 for r0, r1 in b)
+    assert len(b) <= chunks
+    assert tp.chunk_bounds(0, 4) == []
+
+
+def test_packed_swiglu_equals_separate_gate_up():
+    """The packed GEMM's accumulators are the separate gate/up accumulators
+    permuted (bit-identical), and the SwiGLU epilogue on them equals
+    silu(g) * u of the separately scaled values."""
+    import oracle_lib as O
+    rng = np.random.default_rng(0)
+    T, H, il = 64, 128, 256
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    g = (rng.standard_normal((H, il)) * 0.02).astype(np.float32)
+    u = (rng.standard_normal((H, il)) * 0.02).astype(np.float32)
+    xq, sx = O.quantize_rows(x, 0)
+    gq, gs = O.quantize_cols(g, 0)
+    uq, us = O.quantize_cols(u, 0)
+    order = tp.swiglu_pack_order(il)
+    pq = np.ascontiguousarray(np.concatenate([gq, uq], axis=1)[:, order])
+    ps = np.concatenate([gs, us])[order]
+    pq2, ps2 = O.quantize_cols(np.ascontiguousarray(np.concatenate([g, u], axis=1)[:, order]), 0)
+    np.testing.assert_array_equal(pq, pq2)
+    np.testing.assert_array_equal(ps, ps2)
+    acc = O.gemm_fp8_acc(xq, pq, 0, 0, True)
+    ga, ua = O.gemm_fp8_acc(xq, gq, 0, 0, True), O.gemm_fp8_acc(xq, uq, 0, 0, True)
+    np.testing.assert_array_equal(acc, np.concatenate([ga, ua], axis=1)[:, order])
+    h = O.swiglu_epilogue(acc, False, 1.0, sx, ps)
+    gv = ga * sx[:, None] * gs[None, :]
+    uv = ua * sx[:, None] * us[None, :]
+    ref = np.vectorize(lambda a, b: O.lib.orc_silu_mul(float(a), float(b)), otypes=[np.float32])(gv, uv)
+    np.testing.assert_allclose(h, ref, rtol=2e-6, atol=1e-30)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_rank(rank, world, port, case):
+    import torch
+    import torch.distributed as dist
+    import oracle_lib as O
+    from nova_b200 import tp as tpm
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        T, H, I = case
+        rng = np.random.default_rng(7)
+        x = O.f32_to_bf16_bits(rng.standard_normal((T, H)).astype(np.float32))
+        wg = (rng.standard_normal((H, I)) * 0.02).astype(np.float32)
+        wu = (rng.standard_normal((H, I)) * 0.02).astype(np.float32)
+        wd = (rng.standard_normal((I, H)) * 0.02).astype(np.float32)
+        _, part = O.tp_mlp_partial(x, wg, wu, wd, rank, world)
+        out = torch.zeros(T, H, dtype=torch.float32)
+        src = torch.from_numpy(O.bf16_bits_to_f32(part))
+        seen = []
+
+        def compute(r0, r1):
+            seen.append((r0, r1))
+            out[r0:r1] = src[r0:r1]
+            return out[r0:r1]
+
+        tpm.reduce_pipeline(tpm.chunk_bounds(T, 4), compute, None, world)
+        assert seen == tpm.chunk_bounds(T, 4)
+        want = sum(O.bf16_bits_to_f32(O.tp_mlp_partial(x, wg, wu, wd, r, world)[1]) for r in range(world))
+        np.testing.assert_array_equal(out.numpy(), want)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [(600, 256, 512)])
+def test_reduce_pipeline_two_gloo_ranks(case):
+    import torch.multiprocessing as mp
+    mp.start_processes(_gloo_rank, args=(2, _free_port(), case), nprocs=2, join=True, start_method="spawn")
