@@ -144,11 +144,14 @@ nq_status_t nq_calibrate_quantize(const void* src, nq_dtype_t src_dtype, uint8_t
                                   nq_format_t fmt, float* d_amax_scale, nq_stream_t s);
 /* Per-row dynamic quantization (per token of activations, or per output
    channel of an N x K weight): scales[r] = amax(row r)/qmax (1.0 for an
-   all-zero row), q = encode(x / scales[r]).  One launch. */
+   all-zero row), q = encode(x * (qmax / amax(row r))), the reciprocal taken
+   once per row (a row whose qmax / amax overflows float uses
+   q = encode(x / scales[r])).  One launch. */
 nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst, float* scales,
                              int rows, int cols, nq_format_t fmt, nq_stream_t s);
 /* Per-column scales of a rows x cols (K x N) row-major fp32 matrix: the
-   per-output-channel scales of a weight in FP8GEMM's B layout. */
+   per-output-channel scales of a weight in FP8GEMM's B layout (the
+   arithmetic of nq_quantize_rows, per column). */
 nq_status_t nq_quantize_cols(const float* src, uint8_t* dst, float* scales, int rows, int cols,
                              nq_format_t fmt, nq_stream_t s);
 

@@ -344,6 +344,19 @@ struct SplitTail {
 struct Unit {
     int tile, part, kb0, kb1;
 };
+// Tile order of the persistent schedule: bands of P_BAND M-tiles; inside a
+// band the tiles walk N, M fastest.  The clusters in flight at any moment
+// then share at most P_BAND A panels and ~clusters/P_BAND B panels, a working
+// set that stays in L2 when A alone (M x K) does not (M = 16384, K = 8192:
+// 128 MiB), so each operand panel comes from HBM about once per band.
+constexpr int P_BAND = 16;
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
+    const int band = tile / (P_BAND * n_tiles);
+    const int rows = min(P_BAND, m_tiles - band * P_BAND);
+    const int local = tile - band * P_BAND * n_tiles;
+    mb = band * P_BAND + local % rows;
+    nb = local / rows;
+}
 __device__ __forceinline__ Unit decode_unit(int u, const SplitTail& st, int kblocks) {
     if (st.split <= 1 || u < st.full_units) return Unit{u, 0, 0, kblocks};
     const int v = u - st.full_units;
@@ -441,7 +454,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             bool ok = true;
             for (int u = cluster; u < num_units && ok; u += nclusters) {
                 const Unit un = decode_unit(u, st, kblocks);
-                const int mb = un.tile % m_tiles, nb = un.tile / m_tiles;
+                int mb, nb;
+                tile_coords(un.tile, m_tiles, n_tiles, mb, nb);
                 for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
                     if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_STAGE + P_B_STAGE));
@@ -513,7 +527,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             bool ok = mbar_wait(&tfull[acc], acc_phase, err);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const int mb = tile % m_tiles, nb = tile / m_tiles;
+            int mb, nb;
+            tile_coords(tile, m_tiles, n_tiles, mb, nb);
             const int row = mb * P_BM + row_in_tile;
             const bool split_tile = st.split > 1 && tile >= st.full_units;
             const int slot_id = tile - st.full_units;

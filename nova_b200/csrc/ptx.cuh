@@ -104,6 +104,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  "r"(smem_u32(smem_src)), "r"(x), "r"(y)
                  : "memory");
 }
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`
+// (both addresses 16-byte aligned, bytes a multiple of 16; no multicast).
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :
+                 : "r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until at most N bulk groups of this thread still read shared memory.
 template <int N>

@@ -11,9 +11,11 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "codec.cuh"
 #include "nq_internal.h"
+#include "ptx.cuh"
 
 namespace nq {
 
@@ -200,9 +202,49 @@ __global__ void __launch_bounds__(kThreads) k_histogram(const float* __restrict_
     }
 }
 
-// Per-row scaled quantize: scale = amax(row)/qmax (1 for a zero row),
-// q = encode(x / scale).  One block per row; the second pass re-reads the row
-// (from L1/L2: a row is at most a few tens of KB).
+// Per-row / per-column scaling: scale = amax / qmax (1 for an all-zero row)
+// and q = encode(x * inv) with inv = qmax / amax, one IEEE division per row.
+// When qmax / amax overflows (amax < qmax / FLT_MAX) the row is divided by
+// its scale instead, so a row of tiny values never meets an infinite
+// multiplier.  The choice is uniform over a row, so it costs no divergence.
+struct RowScale {
+    float s, inv;
+    bool mul;
+};
+template <int F>
+__device__ __forceinline__ RowScale row_scale(float a) {
+    constexpr float q = dev::FmtTraits<F>::qmax;
+    if (!(a > 0.0f)) return RowScale{1.0f, 1.0f, true};
+    const float inv = q / a;
+    return RowScale{a / q, inv, inv <= FLT_MAX};
+}
+template <bool MUL>
+__device__ __forceinline__ float scale_apply(float x, const RowScale& r) {
+    return MUL ? x * r.inv : x / r.s;
+}
+
+// Element e of a 16-byte vector of fp32 (4) or bf16 (8) values.
+template <class In>
+__device__ __forceinline__ float vec_elem(const uint4& q, int e) {
+    constexpr int EPV = 16 / sizeof(In);
+    const uint32_t w = e < EPV / 4 ? q.x : (e < EPV / 2 ? q.y : (e < 3 * EPV / 4 ? q.z : q.w));
+    if (sizeof(In) == 2) return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
+    return __uint_as_float(w);
+}
+template <int F, class In, bool MUL>
+__device__ __forceinline__ void encode_vec(const uint4& q, uint8_t* out, const RowScale& r) {
+    constexpr int EPV = 16 / sizeof(In);
+    uint32_t codes[EPV / 2];
+#pragma unroll
+    for (int e = 0; e < EPV; e += 2)
+        codes[e / 2] = dev::ocp_encode2<F>(scale_apply<MUL>(vec_elem<In>(q, e), r),
+                                           scale_apply<MUL>(vec_elem<In>(q, e + 1), r));
+    if (EPV == 8) *reinterpret_cast<uint2*>(out) = make_uint2(codes[0] | (codes[1] << 16), codes[2] | (codes[3] << 16));
+    else *reinterpret_cast<uint32_t*>(out) = codes[0] | (codes[1] << 16);
+}
+
+// Per-row scaled quantize, any width and alignment: one block per row; the
+// second pass re-reads the row (from L1/L2).
 template <int F, class In>
 __global__ void __launch_bounds__(kThreads) k_quant_rows(const In* __restrict__ src, uint8_t* __restrict__ dst,
                                                          float* __restrict__ scales, int cols) {
@@ -221,17 +263,22 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows(const In* __restrict__ 
     }
     for (int i = n4 * 4 + threadIdx.x; i < cols; i += blockDim.x) a = fmaxf(a, fabsf(ld1(row + i)));
     a = block_minmax(FLT_MAX, a).y;
-    const float s = a > 0.0f ? a / dev::FmtTraits<F>::qmax : 1.0f;
-    if (threadIdx.x == 0) scales[r] = s;
-    for (int v = threadIdx.x; v < n4; v += blockDim.x) {
-        float x[4];
-        load4<In>(row + 4 * v, x);
-        const uint32_t p0 = dev::ocp_encode2<F>(x[0] / s, x[1] / s);
-        const uint32_t p1 = dev::ocp_encode2<F>(x[2] / s, x[3] / s);
-        reinterpret_cast<uint32_t*>(out)[v] = p0 | (p1 << 16);
-    }
-    for (int i = n4 * 4 + threadIdx.x; i < cols; i += blockDim.x)
-        out[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(ld1(row + i) / s, 0.0f) & 0xFFu);
+    const RowScale rs = row_scale<F>(a);
+    if (threadIdx.x == 0) scales[r] = rs.s;
+    auto pass = [&](auto mul_tag) {
+        constexpr bool MUL = decltype(mul_tag)::value;
+        for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+            float x[4];
+            load4<In>(row + 4 * v, x);
+            const uint32_t p0 = dev::ocp_encode2<F>(scale_apply<MUL>(x[0], rs), scale_apply<MUL>(x[1], rs));
+            const uint32_t p1 = dev::ocp_encode2<F>(scale_apply<MUL>(x[2], rs), scale_apply<MUL>(x[3], rs));
+            reinterpret_cast<uint32_t*>(out)[v] = p0 | (p1 << 16);
+        }
+        for (int i = n4 * 4 + threadIdx.x; i < cols; i += blockDim.x)
+            out[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(scale_apply<MUL>(ld1(row + i), rs), 0.0f) & 0xFFu);
+    };
+    if (rs.mul) pass(std::true_type{});
+    else pass(std::false_type{});
 }
 
 // Per-row scaled quantize with the row held in registers: one read of the
@@ -252,32 +299,88 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows_reg(const In* __restric
         const int idx = threadIdx.x + k * kThreads;
         v[k] = idx < nv ? __ldg(row + idx) : make_uint4(0u, 0u, 0u, 0u);
     }
-    auto elem = [](const uint4& q, int e) -> float {
-        const uint32_t w = e < EPV / 4 ? q.x : (e < EPV / 2 ? q.y : (e < 3 * EPV / 4 ? q.z : q.w));
-        if (sizeof(In) == 2) return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
-        return __uint_as_float(w);
-    };
     float a = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
 #pragma unroll
-        for (int e = 0; e < EPV; ++e) a = fmaxf(a, fabsf(elem(v[k], e)));
+        for (int e = 0; e < EPV; ++e) a = fmaxf(a, fabsf(vec_elem<In>(v[k], e)));
     a = block_minmax(FLT_MAX, a).y;
-    const float s = a > 0.0f ? a / dev::FmtTraits<F>::qmax : 1.0f;
-    if (threadIdx.x == 0) scales[r] = s;
+    const RowScale rs = row_scale<F>(a);
+    if (threadIdx.x == 0) scales[r] = rs.s;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const int idx = threadIdx.x + k * kThreads;
         if (idx >= nv) break;
-        uint32_t codes[EPV / 2];
-#pragma unroll
-        for (int e = 0; e < EPV; e += 2) codes[e / 2] = dev::ocp_encode2<F>(elem(v[k], e) / s, elem(v[k], e + 1) / s);
-        if (EPV == 8) {
-            *reinterpret_cast<uint2*>(out + idx * 8) =
-                make_uint2(codes[0] | (codes[1] << 16), codes[2] | (codes[3] << 16));
-        } else {
-            *reinterpret_cast<uint32_t*>(out + idx * 4) = codes[0] | (codes[1] << 16);
+        if (rs.mul) encode_vec<F, In, true>(v[k], out + idx * EPV, rs);
+        else encode_vec<F, In, false>(v[k], out + idx * EPV, rs);
+    }
+}
+
+// Per-row scaled quantize with rows staged whole in shared memory by 1-D bulk
+// copies: a persistent grid, block b owning rows b, b + gridDim.x, ...; a
+// ring of `stages` row buffers keeps the next rows streaming in from HBM
+// while the current one is reduced and encoded (one HBM read per element,
+// and a block never idles on a single row's load latency).  Row bytes
+// (cols * sizeof(In)) must be a multiple of 16 and src 16-byte aligned.
+template <int F, class In>
+__global__ void __launch_bounds__(kThreads) k_quant_rows_bulk(const In* __restrict__ src, uint8_t* __restrict__ dst,
+                                                              float* __restrict__ scales, int rows, int cols,
+                                                              int stages, uint32_t* err) {
+    extern __shared__ __align__(128) uint8_t q_smem[];
+    constexpr int EPV = 16 / sizeof(In);
+    const uint32_t rb = static_cast<uint32_t>(cols) * sizeof(In);
+    uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + static_cast<size_t>(stages) * rb);
+    const int nv = cols / EPV;
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < stages; ++k) dev::mbar_init(&full[k], 1);
+        dev::fence_mbar_init();
+    }
+    __syncthreads();
+    const char* base = reinterpret_cast<const char*>(src);
+    auto row_of = [&](int i) { return static_cast<long long>(blockIdx.x) + static_cast<long long>(i) * gridDim.x; };
+    auto issue = [&](int i) {
+        const long long r = row_of(i);
+        if (r >= rows) return;
+        const int st = i % stages;
+        dev::mbar_arrive_expect_tx(&full[st], rb);
+        dev::bulk_load_1d(q_smem + static_cast<size_t>(st) * rb, base + r * rb, rb, &full[st]);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < stages; ++i) issue(i);
+    int i = 0;
+    bool ok = true;
+    for (;; ++i) {
+        const long long r = row_of(i);
+        if (r >= rows) break;
+        const int st = i % stages;
+        ok = dev::mbar_wait(&full[st], static_cast<uint32_t>(i / stages) & 1u, err);
+        if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
         }
+        const uint4* buf = reinterpret_cast<const uint4*>(q_smem + static_cast<size_t>(st) * rb);
+        float a = 0.0f;
+        for (int v = threadIdx.x; v < nv; v += kThreads) {
+            const uint4 q = buf[v];
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) a = fmaxf(a, fabsf(vec_elem<In>(q, e)));
+        }
+        a = block_minmax(FLT_MAX, a).y;
+        const RowScale rs = row_scale<F>(a);
+        if (threadIdx.x == 0) scales[r] = rs.s;
+        uint8_t* out = dst + r * cols;
+        if (rs.mul) {
+            for (int v = threadIdx.x; v < nv; v += kThreads) encode_vec<F, In, true>(buf[v], out + v * EPV, rs);
+        } else {
+            for (int v = threadIdx.x; v < nv; v += kThreads) encode_vec<F, In, false>(buf[v], out + v * EPV, rs);
+        }
+        __syncthreads();  // every thread is done with buffer st
+        if (threadIdx.x == 0) issue(i + stages);
+    }
+    if (!ok && threadIdx.x == 0) {
+        // a wait gave up: let the copies still in flight land before the block exits
+        for (int j = i; j < i + stages && row_of(j) < rows; ++j)
+            dev::mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, nullptr);
     }
 }
 
@@ -315,14 +418,55 @@ __global__ void __launch_bounds__(kThreads) k_quant_cols(const float* __restrict
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
         const int c = static_cast<int>(i % cols);
-        const float a = __uint_as_float(__ldg(amax_bits + c));
-        const float s = a > 0.0f ? a / dev::FmtTraits<F>::qmax : 1.0f;
-        if (i < static_cast<size_t>(cols)) scales[c] = s;
-        dst[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(__ldg(src + i) / s, 0.0f) & 0xFFu);
+        const RowScale rs = row_scale<F>(__uint_as_float(__ldg(amax_bits + c)));
+        if (i < static_cast<size_t>(cols)) scales[c] = rs.s;
+        const float x = __ldg(src + i);
+        dst[i] = static_cast<uint8_t>(dev::ocp_encode2<F>(rs.mul ? x * rs.inv : x / rs.s, 0.0f) & 0xFFu);
     }
 }
 
 // ---- host helpers -----------------------------------------------------------------
+}  // namespace
+
+constexpr size_t kBulkRowSmem = 200 * 1024;  // ring budget of one block of k_quant_rows_bulk
+
+// Ring depth: 4 rows up to 16 KB rows, else as many as fit 200 KB (>= 2);
+// grid: every block that fits on the device at once (persistent).
+template <int F>
+nq_status_t launch_quant_rows_bulk(const void* src, nq_dtype_t dt, uint8_t* dst, float* scales, int rows, int cols,
+                                   const DeviceInfo& di, cudaStream_t s) {
+    const size_t rb = static_cast<size_t>(cols) * (dt == NQ_F32 ? 4 : 2);
+    const int stages = rb <= 16384 ? 4 : static_cast<int>(std::min<size_t>(4, kBulkRowSmem / rb));
+    const int smem = static_cast<int>(stages * rb + 8 * stages);
+    auto launch = [&](auto kern, const auto* typed_src) -> nq_status_t {
+        static std::mutex mu;
+        static uint64_t attr_set = 0;
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            const uint64_t bit = 1ull << (di.device & 63);
+            if (!(attr_set & bit)) {
+                NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kBulkRowSmem + 64)),
+                              "cudaFuncSetAttribute(quantize_rows)");
+                attr_set |= bit;
+            }
+        }
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        const int grid = static_cast<int>(std::min<long long>(rows, static_cast<long long>(di.sm_count) * per_sm));
+        kern<<<grid, kThreads, smem, s>>>(typed_src, dst, scales, rows, cols, stages, device_error_word());
+        NQ_LAUNCH_CHECK("nq_quantize_rows (bulk)");
+        return NQ_SUCCESS;
+    };
+    if (dt == NQ_F32) return launch(k_quant_rows_bulk<F, float>, static_cast<const float*>(src));
+    return launch(k_quant_rows_bulk<F, uint16_t>, static_cast<const uint16_t*>(src));
+}
+
+namespace {
+
 bool is_device_pointer(const void* p) {
     cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
@@ -522,8 +666,18 @@ nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst
     nq_status_t st = nq::current_device(&di);
     if (st != NQ_SUCCESS) return st;
     using namespace nq::dev;
-    // register-resident rows: one HBM read per element
     const size_t row_bytes = static_cast<size_t>(cols) * (src_dtype == NQ_F32 ? 4 : 2);
+    // rows of 4 KB .. 100 KB: bulk-staged ring, persistent grid
+    if (row_bytes % 16 == 0 && nq::aligned16(src) && row_bytes >= 4096 && 2 * row_bytes <= nq::kBulkRowSmem &&
+        reinterpret_cast<uintptr_t>(dst) % (src_dtype == NQ_F32 ? 4 : 8) == 0) {
+        switch (fmt) {
+            case NQ_E4M3: return nq::launch_quant_rows_bulk<kE4M3>(src, src_dtype, dst, scales, rows, cols, di, s);
+            case NQ_E5M2: return nq::launch_quant_rows_bulk<kE5M2>(src, src_dtype, dst, scales, rows, cols, di, s);
+            case NQ_INT8: return nq::launch_quant_rows_bulk<kINT8>(src, src_dtype, dst, scales, rows, cols, di, s);
+            default: return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: format");
+        }
+    }
+    // narrower rows, register-resident: one HBM read per element
     const bool reg_ok = row_bytes % 16 == 0 && nq::aligned16(src) && row_bytes <= 4u * 16u * nq::kThreads &&
                         reinterpret_cast<uintptr_t>(dst) % (src_dtype == NQ_F32 ? 4 : 8) == 0;
     if (reg_ok) {

@@ -12,6 +12,7 @@
 #include "oracle.h"
 
 #include <float.h>
+#include <stdlib.h>
 #include <math.h>
 #include <pthread.h>
 #include <string.h>
@@ -397,6 +398,14 @@ void orc_mse_calibrate(const float* data, size_t n, int symmetric, float out[5])
 static float row_scale_of(float amax, int fmt) {
     return amax > 0.0f ? amax / qmax_fmt(fmt) : 1.0f;
 }
+/* Per-row / per-column scaling of the product kernels (reduce.cu row_scale):
+   q = enc(x * inv) with inv = qmax / amax (1 for an all-zero row); when that
+   quotient overflows, the row is divided by its scale instead. */
+static float row_apply(float x, float amax, float scale, int fmt) {
+    if (!(amax > 0.0f)) return x * 1.0f;
+    const float inv = qmax_fmt(fmt) / amax;
+    return inv <= FLT_MAX ? x * inv : x / scale;
+}
 
 void orc_quantize_rows(const void* src, int src_bf16, uint8_t* dst, float* scales,
                        size_t rows, size_t cols, int fmt) {
@@ -412,21 +421,24 @@ void orc_quantize_rows(const void* src, int src_bf16, uint8_t* dst, float* scale
         for (size_t c = 0; c < cols; ++c) {
             float v = src_bf16 ? orc_bf16_to_f32(((const uint16_t*)src)[r * cols + c])
                                : ((const float*)src)[r * cols + c];
-            dst[r * cols + c] = enc_fmt(v / s, fmt);
+            dst[r * cols + c] = enc_fmt(row_apply(v, a, s, fmt), fmt);
         }
     }
 }
 
 void orc_quantize_cols(const float* src, uint8_t* dst, float* scales, size_t rows,
                        size_t cols, int fmt) {
+    float* amax = (float*)malloc((cols ? cols : 1) * sizeof(float));
     for (size_t c = 0; c < cols; ++c) {
         float a = 0.0f;
         for (size_t r = 0; r < rows; ++r) a = mx(a, fabsf(src[r * cols + c]));
+        amax[c] = a;
         scales[c] = row_scale_of(a, fmt);
     }
     for (size_t r = 0; r < rows; ++r)
         for (size_t c = 0; c < cols; ++c)
-            dst[r * cols + c] = enc_fmt(src[r * cols + c] / scales[c], fmt);
+            dst[r * cols + c] = enc_fmt(row_apply(src[r * cols + c], amax[c], scales[c], fmt), fmt);
+    free(amax);
 }
 
 /* ======================================================================

@@ -78,10 +78,12 @@ void orc_histogram_calibrate(const float* data, size_t n, int num_bins, float pe
 void orc_mse_calibrate(const float* data, size_t n, int symmetric, float out[5]);
 
 /* per-row scales: scale[r] = amax(row r)/qmax (1.0 when the row is all zero),
-   q = encode(x / scale[r]).  src is fp32 (src_bf16 == 0) or bf16 bits. */
+   q = encode(x * (qmax / amax)) -- one division per row; a row whose
+   qmax / amax overflows uses q = encode(x / scale[r]).  src is fp32
+   (src_bf16 == 0) or bf16 bits. */
 void orc_quantize_rows(const void* src, int src_bf16, uint8_t* dst, float* scales,
                        size_t rows, size_t cols, int fmt);
-/* per-column scales of a row-major rows x cols matrix */
+/* per-column scales of a row-major rows x cols matrix (same arithmetic per column) */
 void orc_quantize_cols(const float* src, uint8_t* dst, float* scales, size_t rows,
                        size_t cols, int fmt);
 

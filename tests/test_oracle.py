@@ -169,7 +169,16 @@ def test_rows_cols_quantize_oracle_consistency():
     x = rng.standard_normal((9, 40)).astype(np.float32)
     q, s = O.quantize_rows(x, 0)
     for r in range(9):
-        assert s[r] == np.float32(np.abs(x[r]).max()) / np.float32(448.0)
-        np.testing.assert_array_equal(q[r], O.quantize_ocp(x[r], float(s[r]), 0))
+        amax = np.float32(np.abs(x[r]).max())
+        assert s[r] == amax / np.float32(448.0)
+        inv = np.float32(448.0) / amax
+        np.testing.assert_array_equal(q[r], O.quantize_ocp((x[r] * inv).astype(np.float32), 1.0, 0))
+    # a row of tiny values: qmax / amax overflows, the row is divided by its scale
+    tiny = np.array([[1e-39, -5e-40, 0.0, 2.5e-40]], np.float32)
+    qt, st = O.quantize_rows(tiny, 0)
+    assert np.isinf(np.float32(448.0) / np.float32(1e-39))
+    np.testing.assert_array_equal(qt[0], O.quantize_ocp(tiny[0], float(st[0]), 0))
+    z, sz = O.quantize_rows(np.zeros((1, 8), np.float32), 0)
+    assert sz[0] == 1.0 and not z.any()
     qc, sc = O.quantize_cols(x, 2)
     np.testing.assert_array_equal(qc.T, O.quantize_rows(np.ascontiguousarray(x.T), 2)[0])

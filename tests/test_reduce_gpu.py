@@ -110,13 +110,20 @@ def test_amax_scale_and_calibrate_quantize(nq, fmt, bf16):
 
 @pytest.mark.parametrize("fmt", [0, 2])
 @pytest.mark.parametrize("bf16", [False, True])
-@pytest.mark.parametrize("shape", [(7, 33), (64, 4096), (3, 16)])
+@pytest.mark.parametrize("shape", [(7, 33), (64, 4096), (3, 16), (300, 8192), (50, 28672), (20, 28672),
+                                   (1000, 2048), (5, 1024)])
 def test_quantize_rows(nq, fmt, bf16, shape):
+    """All row-width regimes: unaligned/odd widths (two-pass kernel), rows
+    under 4 KB (register-resident), 4 KB .. 100 KB (bulk-staged ring; 28672
+    bf16 = 56 KB takes 3 stages) and fp32 rows over 100 KB (two-pass).  Row 1
+    holds tiny values whose qmax / amax overflows (the division path)."""
     import oracle_lib as O
     from gpu_util import dev, empty, host, ptr, stream
     r, c = shape
     x = rand(r * c, r * 31 + c, 1.0).reshape(r, c)
     x[0, : min(c, 5)] *= 20.0
+    if r > 1:
+        x[1] *= np.float32(1e-39)
     if r > 2:
         x[2] = 0.0
     if bf16:
