@@ -189,10 +189,11 @@ class RowParallelLayer:
     [batch*seq x in_features/tp] this rank's shard, output [batch*seq x
     out_features] replicated after the sum all-reduce (bf16, chunked)."""
 
-    def __init__(self, in_features: int, out_features: int, group=None, chunks: int = 4):
+    def __init__(self, in_features: int, out_features: int, group=None, chunks=None):
         import torch
-        self.torch, self.group, self.chunks = torch, group, chunks
+        self.torch, self.group = torch, group
         self.rank, self.tp = _group_info(group)
+        self.chunks = chunks if chunks is not None else (4 if self.tp > 1 else 1)
         if in_features % self.tp:
             raise ValueError("in_features must be divisible by the TP degree")
         self.in_features, self.out_features = in_features, out_features
@@ -216,7 +217,7 @@ class RowParallelLayer:
             self.lin.gemm(xq, sx, output, r0, r1)
             return output[r0:r1]
 
-        reduce_pipeline(chunk_bounds(T, self.chunks if self.tp > 1 else 1), compute, self.group, self.tp)
+        reduce_pipeline(chunk_bounds(T, self.chunks), compute, self.group, self.tp)
         if sync:
             self.torch.cuda.current_stream().synchronize()
         return output
@@ -232,7 +233,7 @@ class TensorParallelMLP:
     shard are one packed FP8 weight (alternating 128-column blocks) so one
     GEMM with the SwiGLU epilogue produces silu(g) * u directly."""
 
-    def __init__(self, hidden_dim: int, intermediate_size: int, group=None, chunks: int = 4,
+    def __init__(self, hidden_dim: int, intermediate_size: int, group=None, chunks=None,
                  overlap: str = "full"):
         import torch
         if overlap not in ("full", "down"):
@@ -245,9 +246,11 @@ class TensorParallelMLP:
             raise ValueError("hidden_dim must be a multiple of 16")
         self.H, self.I = hidden_dim, intermediate_size
         self.I_local = intermediate_size // self.tp
-        self.chunks = chunks
+        # token chunks of the GEMM / all-reduce pipeline: 4 when there is an
+        # all-reduce to overlap, else 1 (an explicit value is always honoured)
+        self.chunks = chunks if chunks is not None else (4 if self.tp > 1 else 1)
         self.gate_up = _FP8Linear()
-        self.down = RowParallelLayer(intermediate_size, hidden_dim, group, chunks)
+        self.down = RowParallelLayer(intermediate_size, hidden_dim, group, self.chunks)
         self._h = {}
 
     def set_weight(self, gate_weight, up_weight, down_weight):
@@ -281,7 +284,7 @@ class TensorParallelMLP:
         epi = self.gate_up.nq.EPI_SWIGLU
         down = self.down.lin
         xq, sx = self.gate_up.act(input, T)
-        bounds = chunk_bounds(T, self.chunks if self.tp > 1 else 1)
+        bounds = chunk_bounds(T, self.chunks)
         if self.overlap == "down" or len(bounds) == 1:
             self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)
 

@@ -283,7 +283,14 @@ def tp_mlp_partial(x_bits, wg, wu, wd, rank, tp):
     gu = np.ascontiguousarray(np.concatenate([g, u], axis=1)[:, order])
     gq, gs = quantize_cols(gu, 0)
     h = swiglu_epilogue(gemm_fp8_acc(xq, gq, 0, 0, True), True, 1.0, sx, gs)
-    hq, sh = quantize_rows(h, 0, bf16=True)
+    return h, tp_down_partial(h, wd, rank, tp)
+
+
+def tp_down_partial(h_bits, wd, rank, tp):
+    """The row-parallel half of tp_mlp_partial: per-token quantize of this
+    rank's h (bf16 bits, T x I/tp), down row shard with per-column scales,
+    bf16 partial (T x H)."""
+    il = wd.shape[0] // tp
+    hq, sh = quantize_rows(np.ascontiguousarray(h_bits), 0, bf16=True)
     dq, ds = quantize_cols(np.ascontiguousarray(wd[rank * il:(rank + 1) * il]), 0)
-    part = epilogue(gemm_fp8_acc(hq, dq, 0, 0, True), True, 1.0, sh, ds)
-    return h, part
+    return epilogue(gemm_fp8_acc(hq, dq, 0, 0, True), True, 1.0, sh, ds)

@@ -1,9 +1,15 @@
 """Tensor-parallel FP8 layers and the SwiGLU MLP on the GPU against the
-oracle's restatement (oracle_lib.tp_mlp_partial).  tp = 1 runs in this
-process; tp = 2 runs tests/tp_worker.py under torchrun over NCCL when the
-box has two GPUs.  Tolerances: the SwiGLU intermediate h (bf16) within
-1e-2 relative (the FP8 bar), the MLP output within 2e-2 (h's bf16 rounding
-can move single FP8 codes of the second quantization)."""
+oracle's restatement (oracle_lib.tp_mlp_partial / tp_down_partial).  tp = 1
+runs in this process; tp = 2 runs tests/tp_worker.py under torchrun over
+NCCL when the box has two GPUs.
+
+Tolerances.  The SwiGLU intermediate h (bf16) and the output computed from
+the GPU's own h (oracle_lib.tp_down_partial) are within 1e-2 per element
+(max relative error, |ref| floored at 1e-2 rms): only the accumulation order
+and one bf16 rounding differ.  Against the all-oracle pipeline the output is
+compared normwise (1e-2): a 1-ulp bf16 difference in h can move single FP8
+codes of the second quantization, a per-element effect the norm averages.
+"""
 import os
 import subprocess
 import sys
@@ -44,21 +50,45 @@ def bits(t):
     return t.cpu().view(torch.int16).numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("T,H,I,overlap", [(300, 256, 512, "full"), (512, 512, 1024, "down"), (64, 256, 256, "full")])
-def test_tp1_mlp_vs_oracle(cuda, T, H, I, overlap):
-    import torch
+def norm_err(got, ref):
+    got = got.astype(np.float64)
+    ref = ref.astype(np.float64)
+    return float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+
+
+def check_mlp(got_bits, h_bits_per_rank, x, wg, wu, wd, tp):
+    """Returns (max h error, output error vs the GPU-h oracle, normwise
+    output error vs the all-oracle pipeline).  The second is taken relative
+    to sum_r |partial_r| per element (floored at 1e-2 of its rms): the
+    condition of a sum whose terms may cancel."""
     import oracle_lib as O
+    h_err, from_h, mag, full = 0.0, 0.0, 0.0, 0.0
+    for r in range(tp):
+        h_ref, part = O.tp_mlp_partial(x, wg, wu, wd, r, tp)
+        h_err = max(h_err, rel_err(O.bf16_bits_to_f32(h_bits_per_rank[r]), O.bf16_bits_to_f32(h_ref)))
+        p = O.bf16_bits_to_f32(O.tp_down_partial(h_bits_per_rank[r], wd, r, tp)).astype(np.float64)
+        from_h, mag = from_h + p, mag + np.abs(p)
+        full = full + O.bf16_bits_to_f32(part).astype(np.float64)
+    got = O.bf16_bits_to_f32(got_bits).astype(np.float64)
+    floor = 1e-2 * np.sqrt(np.mean(mag * mag)) + 1e-30
+    out_err = float(np.max(np.abs(got - from_h) / np.maximum(mag, floor)))
+    return h_err, out_err, norm_err(got, full)
+
+
+@pytest.mark.parametrize("T,H,I,overlap,chunks", [(300, 256, 512, "full", None), (512, 512, 1024, "down", 3),
+                                                  (600, 256, 512, "full", 3), (64, 256, 256, "full", 4)])
+def test_tp1_mlp_vs_oracle(cuda, T, H, I, overlap, chunks):
+    import torch
     import nova_b200.capi as nq
     from nova_b200.tp import TensorParallelMLP
     x, wg, wu, wd = weights(T, H, I)
-    mlp = TensorParallelMLP(H, I, overlap=overlap)
+    mlp = TensorParallelMLP(H, I, overlap=overlap, chunks=chunks)
     mlp.set_weight(wg, wu, wd)
     xin = to_dev_bf16(x)
     out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     mlp.forward(xin, out, 1, T)
-    h_ref, out_ref = O.tp_mlp_partial(x, wg, wu, wd, 0, 1)
-    assert rel_err(O.bf16_bits_to_f32(bits(mlp._h[T])), O.bf16_bits_to_f32(h_ref)) <= 1e-2
-    assert rel_err(O.bf16_bits_to_f32(bits(out)), O.bf16_bits_to_f32(out_ref)) <= 2e-2
+    h_err, out_err, full_err = check_mlp(bits(out), [bits(mlp._h[T])], x, wg, wu, wd, 1)
+    assert h_err <= 1e-2 and out_err <= 1e-2 and full_err <= 1e-2, (h_err, out_err, full_err)
     assert nq.device_error_flags() == 0
 
 
