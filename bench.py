@@ -289,7 +289,7 @@ def run_ours(args):
     tp_res = None
     if not args.no_tp_mlp:
         tp_res = tp_mlp_bench(world, rank, max(3, min(args.steps, 10)), args.warmup if args.warmup < 5 else 5,
-                              chunks=args.tp_chunks, overlap=args.tp_overlap)
+                              chunks=args.tp_chunks, overlap=args.tp_overlap, allreduce=args.tp_allreduce)
 
     if rank != 0:
         if world > 1:
@@ -378,7 +378,7 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20)):
     return out
 
 
-def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4, overlap="full"):
+def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4, overlap="full", allreduce="auto"):
     """the FP8 SwiGLU MLP (nova_b200.tp.TensorParallelMLP)
     with tp = world size, T tokens per step (strong scaling: the same T at
     every tp).  x ~ N(0,1) bf16, weights ~ N(0,0.02) fp32 generated on the
@@ -386,11 +386,14 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4,
     quantized by set_weight.  One step = forward() (per-token quantize,
     gate/up GEMM + SwiGLU, quantize, down GEMM, chunked bf16 NCCL
     all-reduce); time = max over ranks of the CUDA-event time of `steps`
-    forwards.  Inputs (256 MiB) and weights exceed L2."""
+    forwards.  Inputs (256 MiB) and weights exceed L2.  allreduce "auto" /
+    "nvls" / "p2p": the down GEMM and the all-reduce are one kernel
+    (nq_gemm_allreduce) and forward returns the symmetric output buffer;
+    "nccl": chunked GEMM + torch.distributed all_reduce into `out`."""
     import torch
     from nova_b200.tp import TensorParallelMLP
     g = torch.Generator(device="cuda").manual_seed(11)
-    mlp = TensorParallelMLP(H, I, chunks=chunks, overlap=overlap)
+    mlp = TensorParallelMLP(H, I, chunks=chunks, overlap=overlap, allreduce=allreduce)
     wg = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
     wu = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
     wd = torch.randn(I, H, device="cuda", generator=g).mul_(0.02)
@@ -398,7 +401,8 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4,
     del wg, wu, wd
     torch.cuda.empty_cache()
     x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
-    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    fused = mlp.down.fused is not None
+    out = None if fused else torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     for _ in range(warmup):
         mlp.forward(x, out, 1, T, sync=False)
     torch.cuda.synchronize()
@@ -417,7 +421,9 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4,
     fp8_peak = 2.0 * pk["bf16_tflops"]
     tflops = flops / (ms * 1e-3) / 1e12
     res = {"workload": "tp_fp8_swiglu_mlp (BASELINE configs[4])", "tokens": T, "hidden": H, "intermediate": I,
-           "tp": world, "chunks": chunks, "overlap": overlap, "ms_per_step": round(ms, 4),
+           "tp": world, "allreduce": (("fused-nvls" if mlp.down.fused.multicast else "fused-p2p") if fused
+                                      else ("nccl" if world > 1 else "none")),
+           "chunks": chunks if not fused else 1, "overlap": overlap, "ms_per_step": round(ms, 4),
            "tokens_per_s": T / (ms * 1e-3), "tflops_total": tflops,
            "frac_of_tp_x_fp8_peak": tflops / (world * fp8_peak),
            "allreduce_bytes": 2 * T * H if world > 1 else 0, "scaling": "strong"}
@@ -466,6 +472,7 @@ def main():
     ap.add_argument("--no-tp-mlp", action="store_true", help="skip the TP SwiGLU MLP (configs[4]) block")
     ap.add_argument("--tp-chunks", type=int, default=4)
     ap.add_argument("--tp-overlap", choices=["full", "down"], default="full")
+    ap.add_argument("--tp-allreduce", choices=["auto", "nvls", "p2p", "nccl"], default="auto")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

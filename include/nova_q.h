@@ -214,6 +214,49 @@ nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, vo
 nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out,
                          nq_stream_t s);
 
+/* ---- GEMM fused with the all-reduce of a row-parallel layer ------------------
+ * The down projection of a tensor-parallel MLP (RowParallelLayer::forward,
+ * tensor_parallel_layers.cpp:370-416: a GEMM on the rank's K shard, then
+ * ncclAllReduce(sum) of the M x N output, :406) as ONE kernel per rank.  Every
+ * rank writes its bf16 partial tile to its `partial` buffer and raises the
+ * tile's counter on the tile's owner (rank = tile % tp).  Inside the same
+ * kernel the owner's reducer warps wait for all tp partials of each owned
+ * tile, sum them and write the sum to every rank's `out`:
+ *   multicast (mc_partial/mc_out/mc_done non-NULL): multimem.ld_reduce
+ *     (fp32 accumulation in the NVSwitch, one bf16 rounding) and multimem.st;
+ *   peer (multicast NULL): loads of the tp partials through the peer
+ *     pointers, fp32 sum in rank order, one bf16 rounding, stores to each
+ *     peer's `out`.
+ * The kernel returns when this rank's `out` holds every tile, so `out` is
+ * complete on the stream afterwards.  All buffers are symmetric allocations
+ * (same size on every rank, mapped into every peer); `flags` (at least
+ * nq_gemm_allreduce_counters(m, n) words) and `done` must be zero before the
+ * first call and are left zero by every successful call.  Every rank must make
+ * the same sequence of calls with the same m, n.  Waits on other GPUs give up
+ * after 5 s and set the device error word (nq_device_error_flags).
+ * Requirements: desc->out_dtype NQ_BF16, desc->epilogue NQ_EPI_NONE,
+ * n % 256 == 0, k % 16 == 0, 1 <= tp <= NQ_MAX_TP. */
+#define NQ_MAX_TP 8
+typedef struct {
+    int tp, rank;
+    void* partial;       /* this rank's M x N bf16 partial buffer */
+    void* out;           /* this rank's M x N bf16 output buffer */
+    void* mc_partial;    /* multicast address of the partial buffers, or NULL */
+    void* mc_out;        /* multicast address of the output buffers, or NULL */
+    uint32_t* mc_done;   /* multicast address of the completion counters, or NULL */
+    uint32_t* flags;     /* this rank's per-tile arrival counters */
+    uint32_t* done;      /* this rank's completion counter */
+    uint32_t* peer_flags[NQ_MAX_TP];   /* every rank's `flags` (this rank's included) */
+    void* peer_partial[NQ_MAX_TP];     /* peer path: every rank's `partial` */
+    void* peer_out[NQ_MAX_TP];         /* peer path: every rank's `out` */
+    uint32_t* peer_done[NQ_MAX_TP];    /* peer path: every rank's `done` */
+} nq_allreduce_desc_t;
+
+/* Per-tile counters nq_gemm_allreduce needs for an m x n output. */
+int nq_gemm_allreduce_counters(int m, int n);
+nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* desc, const nq_allreduce_desc_t* ar,
+                              const void* a, const void* b, nq_stream_t s);
+
 /* FP8GEMM::forward / forward_async, include/cuda/quantize/fp8_gemm.hpp:55-69
    (fp8_gemm.cu:164-198): fp32 out = scale_out * sum (a*scale_a)(b*scale_b),
    A M x K, B K x N, E4M3 codes read as OCP E4M3FN by the tensor cores. */

@@ -37,6 +37,17 @@ class GemmDesc(C.Structure):
                 ("col_scale", C.c_void_p), ("bias", C.c_void_p), ("epilogue", C.c_int)]
 
 
+MAX_TP = 8
+
+
+class AllreduceDesc(C.Structure):
+    _fields_ = [("tp", C.c_int), ("rank", C.c_int), ("partial", C.c_void_p), ("out", C.c_void_p),
+                ("mc_partial", C.c_void_p), ("mc_out", C.c_void_p), ("mc_done", C.c_void_p),
+                ("flags", C.c_void_p), ("done", C.c_void_p),
+                ("peer_flags", C.c_void_p * MAX_TP), ("peer_partial", C.c_void_p * MAX_TP),
+                ("peer_out", C.c_void_p * MAX_TP), ("peer_done", C.c_void_p * MAX_TP)]
+
+
 _SIGS = {
     "nq_quantize_f32_to_fp8e4m3": [_p, _p, _sz, _p],
     "nq_quantize_f32_to_fp8e5m2": [_p, _p, _sz, _p],
@@ -61,6 +72,7 @@ _SIGS = {
     "nq_quantize_cols_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "nq_gemm": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_gemm_simt": [C.POINTER(GemmDesc), _p, _p, _p, _p],
+    "nq_gemm_allreduce": [C.POINTER(GemmDesc), C.POINTER(AllreduceDesc), _p, _p, _p],
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_fp8e5m2_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_device_error_flags": [_u32p, _i],
@@ -74,6 +86,9 @@ lib.nq_last_error.argtypes = []
 lib.nq_version.restype = C.c_int
 lib.nq_fp8_gemm_workspace_size.restype = C.c_size_t
 lib.nq_fp8_gemm_workspace_size.argtypes = [_i, _i, _i]
+lib.nq_gemm_allreduce_counters.restype = C.c_int
+lib.nq_gemm_allreduce_counters.argtypes = [_i, _i]
+gemm_allreduce_counters = lib.nq_gemm_allreduce_counters
 
 
 def _wrap(name, argtypes):
@@ -98,7 +113,8 @@ for _n, _a in _SIGS.items():
 
 
 def exported_symbols():
-    return sorted(list(_SIGS) + ["nq_status_string", "nq_last_error", "nq_version", "nq_fp8_gemm_workspace_size"])
+    return sorted(list(_SIGS) + ["nq_status_string", "nq_last_error", "nq_version", "nq_fp8_gemm_workspace_size",
+                                 "nq_gemm_allreduce_counters"])
 
 
 EPI_NONE, EPI_SWIGLU = 0, 1

@@ -52,6 +52,22 @@ struct Epi {
     const float* bias;
 };
 
+// Device view of nq_allreduce_desc_t: the all-reduce epilogue of k_gemm_tc2.
+struct ArParams {
+    int tp, rank;
+    uint8_t* mc_partial;
+    uint8_t* mc_out;
+    uint32_t* mc_done;
+    uint32_t* flags;
+    uint32_t* done;
+    uint32_t* peer_flags[NQ_MAX_TP];
+    const uint8_t* peer_partial[NQ_MAX_TP];
+    uint8_t* peer_out[NQ_MAX_TP];
+    uint32_t* peer_done[NQ_MAX_TP];
+};
+// Upper bound of a wait on another GPU (its kernel may start a little later).
+constexpr uint64_t kPeerWaitLimitNs = 5000000000ull;
+
 // Per-chunk column operands of the epilogue: lane j holds column (col0 + j)'s
 // scale and bias, or the exact identities 1.0 and -0.0 when absent
 // (x * 1 == x and x + (-0) == x for every x, signed zeros included), so the
@@ -378,6 +394,19 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t wan
     }
 }
 
+// Spins (bounded by `limit` ns) until the system-scope value at p >= want.
+__device__ __forceinline__ bool wait_sys_geq(const uint32_t* p, uint32_t want, uint32_t* err, uint64_t limit) {
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(p) < want) {
+        if (globaltimer() - t0 > limit) {
+            if (err) atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+        __nanosleep(128);
+    }
+    return true;
+}
+
 // Epilogue staging: per epilogue warp two 4 KB slots, each one 32 x 32 output
 // chunk (rows of 128 B for 4-byte outputs, 64 B for bf16), swizzled so that
 // the row-per-lane writes are bank-conflict free; a TMA store per chunk.
@@ -386,15 +415,107 @@ constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_SLOT;
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
 
 
+// Owner side of the fused all-reduce, run by one warp per cluster (warp 1 of
+// the pair's second CTA, idle in the GEMM).  For every tile this cluster
+// computes and this rank owns (tile % tp == rank): wait until all tp ranks'
+// 16 epilogue warps have stored their partial of the tile, sum the tp partials
+// (multicast: multimem.ld_reduce with fp32 accumulation in the switch; peer:
+// fp32 sum in rank order), write the bf16 sum to every rank's output, reset
+// the tile's counter and count the tile on every rank's completion counter.
+// Cluster 0 then waits until this rank's output holds all tiles.  32 lanes
+// cover the 512 bytes of one tile row; 8 (multicast) or 4 (peer) rows in flight.
+__device__ __forceinline__ void ar_reduce(const ArParams& ar, int cluster, int nclusters, int m_tiles, int n_tiles,
+                                          int M, int N, uint32_t* err) {
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = m_tiles * n_tiles;
+    const uint32_t want = static_cast<uint32_t>(ar.tp) * (2 * P_EPI_WARPS);
+    const size_t pitch = static_cast<size_t>(N) * 2;
+    bool ok = true;
+    for (int t = cluster; t < num_tiles; t += nclusters) {
+        if (t % ar.tp != ar.rank) continue;
+        if (lane == 0) ok = wait_sys_geq(ar.flags + t, want, err, kPeerWaitLimitNs);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        int mb, nb;
+        tile_coords(t, m_tiles, n_tiles, mb, nb);
+        const int r0 = mb * P_BM;
+        const int rows = min(P_BM, M - r0);
+        const size_t base = static_cast<size_t>(r0) * pitch + static_cast<size_t>(nb) * P_BN * 2 + lane * 16;
+        if (ar.mc_partial) {
+            for (int r = 0; r < rows; r += 8) {
+                uint4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (r + u < rows) v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u) * pitch);
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (r + u < rows) multimem_st_v4(ar.mc_out + base + (r + u) * pitch, v[u]);
+            }
+        } else {
+            for (int r = 0; r < rows; r += 4) {
+                float acc[4][8];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[u][e] = 0.0f;
+                for (int p = 0; p < ar.tp; ++p) {
+                    uint4 q[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (r + u < rows)
+                            q[u] = __ldcg(reinterpret_cast<const uint4*>(ar.peer_partial[p] + base + (r + u) * pitch));
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if (r + u >= rows) continue;
+                        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            acc[u][2 * e] = __fadd_rn(acc[u][2 * e], __uint_as_float(w[e] << 16));
+                            acc[u][2 * e + 1] = __fadd_rn(acc[u][2 * e + 1], __uint_as_float(w[e] & 0xFFFF0000u));
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (r + u >= rows) continue;
+                    const uint4 o = make_uint4(f32x2_to_bf16x2(acc[u][0], acc[u][1]), f32x2_to_bf16x2(acc[u][2], acc[u][3]),
+                                               f32x2_to_bf16x2(acc[u][4], acc[u][5]), f32x2_to_bf16x2(acc[u][6], acc[u][7]));
+                    for (int p = 0; p < ar.tp; ++p)
+                        __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u) * pitch), o);
+                }
+            }
+        }
+        // every arrival of this call is in: the counter is free for the next call
+        if (lane == 0) ar.flags[t] = 0u;
+        fence_acq_rel_sys();
+        __syncwarp();
+        if (lane == 0) {
+            if (ar.mc_done) multimem_red_add_release(ar.mc_done, 1u);
+            else
+                for (int p = 0; p < ar.tp; ++p) red_add_release_sys(ar.peer_done[p], 1u);
+        }
+    }
+    if (cluster == 0 && lane == 0 && ok) {
+        // the last arrival of this call: the counter is free for the next call
+        if (wait_sys_geq(ar.done, static_cast<uint32_t>(num_tiles), err, kPeerWaitLimitNs)) {
+            *reinterpret_cast<volatile uint32_t*>(ar.done) = 0u;
+            fence_acq_rel_sys();
+        }
+    }
+}
+
 // OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
 // 1 = bf16 through TMA stores, 2 = int8 requantized, direct stores.
 // SWIGLU: columns [0,128) of each 256-wide tile are gate, [128,256) up; the
 // tile writes 128 columns of silu(g) * u.
-template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU>
+// AR: the partial tile goes to this rank's partial buffer (tmC) and the
+// tile's owner reduces it across ranks (ar_reduce); bf16 output only.
+template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU, bool AR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
-               uint32_t* err) {
+               const __grid_constant__ ArParams ar, uint32_t* err) {
+    static_assert(!AR || (OUTK == 1 && !SWIGLU), "the all-reduce epilogue writes bf16 tiles");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -473,6 +594,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA only) ----------------
+        if constexpr (AR) {
+            // the second CTA's warp 1 reduces the tiles this rank owns
+            if (rank == 1) ar_reduce(ar, cluster, nclusters, m_tiles, n_tiles, M, N, err);
+        }
         if (rank == 0 && elect_one()) {
             int stage = 0;
             uint32_t phase = 0;
@@ -726,6 +851,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                     bulk_commit_group();
                 }
                 ++chunk_seq;
+            }
+            if constexpr (AR) {
+                // this warp's part of the partial tile is in memory: count it on the owner
+                if (lane == 0) {
+                    bulk_wait_group_all();
+                    fence_proxy_async_global();
+                    red_add_release_sys(ar.peer_flags[tile % ar.tp] + tile, 1u);
+                }
+                __syncwarp();
             }
         }
         if (lane == 0) bulk_wait_group_all();
@@ -1082,9 +1216,9 @@ nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
     return NQ_SUCCESS;
 }
 
-template <bool I8, bool KN, int OUTK, bool SWIGLU = false>
+template <bool I8, bool KN, int OUTK, bool SWIGLU = false, bool AR = false>
 nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, void* out, const Epi& ep,
-                       cudaStream_t s, const DeviceInfo& di) {
+                       cudaStream_t s, const DeviceInfo& di, const ArParams* arp = nullptr) {
     CUtensorMap ma, mb, mc;
     nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, 128);
     if (st != NQ_SUCCESS) return st;
@@ -1100,7 +1234,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     }
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
-    auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU>;
+    auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU, AR>;
     static uint64_t attr_set = 0;
     st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
@@ -1127,7 +1261,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     const int rem = tiles % clusters;
     // Splitting pays off only when a tile's MMA time clearly exceeds its
     // epilogue (part 0's epilogue waits for part 1's): long K only.
-    const int split = (!SWIGLU && rem && clusters / rem >= 2 && kblocks >= 48) ? 2 : 1;
+    const int split = (!SWIGLU && !AR && rem && clusters / rem >= 2 && kblocks >= 48) ? 2 : 1;
     void* scratch = nullptr;
     if (split >= 2) {
         tail.full_units = tiles - rem;
@@ -1145,7 +1279,10 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
         }
     }
     uint32_t* err = device_error_word();
-    kern<<<grid, P_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, err);
+    ArParams ar;
+    if (arp) ar = *arp;
+    else std::memset(&ar, 0, sizeof(ar));
+    kern<<<grid, P_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, ar, err);
     cudaError_t e = cudaGetLastError();
     if (scratch) scratch_free(scratch, s);
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
@@ -1298,12 +1435,75 @@ nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, voi
     return NQ_SUCCESS;
 }
 
+nq_status_t gemm_allreduce_impl(const nq_gemm_desc_t* d, const nq_allreduce_desc_t* r, const void* a, const void* b,
+                                cudaStream_t s) {
+    if (!d || !r) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: null descriptor");
+    if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: sizes must be positive");
+    if (!a || !b) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: null operand");
+    const bool i8 = d->a_format == NQ_INT8;
+    if (i8 != (d->b_format == NQ_INT8)) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: INT8 needs both operands INT8");
+    if (d->a_format < NQ_E4M3 || d->a_format > NQ_INT8 || d->b_format < NQ_E4M3 || d->b_format > NQ_INT8)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: format");
+    if (d->b_layout != NQ_B_KN && d->b_layout != NQ_B_NK) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: b_layout");
+    if (d->out_dtype != NQ_BF16 || d->epilogue != NQ_EPI_NONE)
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: bf16 output without a fused activation only");
+    if (d->n % P_BN != 0 || d->k % 16 != 0 || !aligned16(a) || !aligned16(b))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: needs n % 256 == 0, k % 16 == 0, 16-byte aligned operands");
+    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: tp / rank");
+    if (!r->partial || !r->out || !r->flags || !r->done || !aligned16(r->partial) || !aligned16(r->out))
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: partial / out / flags / done");
+    const bool mc = r->mc_partial != nullptr;
+    if (mc && (!r->mc_out || !r->mc_done || !aligned16(r->mc_partial) || !aligned16(r->mc_out)))
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: multicast addresses");
+    for (int p = 0; p < r->tp; ++p) {
+        if (!r->peer_flags[p]) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: peer_flags");
+        if (!mc && (!r->peer_partial[p] || !r->peer_out[p] || !r->peer_done[p] || !aligned16(r->peer_partial[p]) ||
+                    !aligned16(r->peer_out[p])))
+            return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: peer pointers");
+    }
+    DeviceInfo di;
+    nq_status_t st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    ArParams ar;
+    std::memset(&ar, 0, sizeof(ar));
+    ar.tp = r->tp;
+    ar.rank = r->rank;
+    ar.mc_partial = static_cast<uint8_t*>(r->mc_partial);
+    ar.mc_out = static_cast<uint8_t*>(r->mc_out);
+    ar.mc_done = r->mc_done;
+    ar.flags = r->flags;
+    ar.done = r->done;
+    for (int p = 0; p < r->tp; ++p) {
+        ar.peer_flags[p] = r->peer_flags[p];
+        ar.peer_partial[p] = static_cast<const uint8_t*>(r->peer_partial[p]);
+        ar.peer_out[p] = static_cast<uint8_t*>(r->peer_out[p]);
+        ar.peer_done[p] = r->peer_done[p];
+    }
+    Epi ep{r->partial, d->n, NQ_BF16, d->alpha, d->row_scale, d->col_scale, d->bias};
+    const bool kn = d->b_layout == NQ_B_KN;
+    if (i8) return kn ? launch_tc2<true, true, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar)
+                      : launch_tc2<true, false, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar);
+    return kn ? launch_tc2<false, true, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar)
+              : launch_tc2<false, false, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar);
+}
+
 }  // namespace nq
 
 extern "C" {
 
 nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out, nq_stream_t s) {
     return nq::gemm_impl(desc, a, b, out, s, 0);
+}
+
+int nq_gemm_allreduce_counters(int m, int n) {
+    if (m <= 0 || n <= 0) return 0;
+    return ((m + nq::P_BM - 1) / nq::P_BM) * ((n + nq::P_BN - 1) / nq::P_BN);
+}
+
+nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* d, const nq_allreduce_desc_t* a_r, const void* a, const void* b,
+                              nq_stream_t s) {
+    return nq::gemm_allreduce_impl(d, a_r, a, b, s);
 }
 
 // Test hook: the same GEMM forced onto the SIMT kernel (exact sequential-k).

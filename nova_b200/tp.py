@@ -100,6 +100,96 @@ def _as_tensor(w):
     return w if isinstance(w, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(w, np.float32))
 
 
+# ---- fused GEMM + all-reduce over peer memory -------------------------------------
+class SymmetricAllReduce:
+    """Symmetric buffers (torch.distributed._symmetric_memory: the same
+    allocation mapped into every rank of `group`, plus an NVSwitch multicast
+    mapping when the box has one) for nq_gemm_allreduce: per output shape a
+    bf16 partial and a bf16 output buffer, and the per-tile arrival counters
+    and the completion counter, zeroed once.  mode "nvls" reduces through
+    multimem (needs multicast), "p2p" through peer loads and stores, "auto"
+    picks nvls when multicast is present."""
+
+    def __init__(self, group=None, mode: str = "auto"):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        from . import capi
+        self.torch, self.dist, self.symm, self.nq = torch, dist, symm, capi
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank, self.tp = dist.get_rank(self.group), dist.get_world_size(self.group)
+        if self.tp > capi.MAX_TP:
+            raise ValueError(f"the fused all-reduce supports up to {capi.MAX_TP} ranks")
+        self.mode = mode
+        self._shapes = {}
+        self._ctrl = None
+
+    def _map(self, t):
+        """(local, [peer pointers], multicast pointer or 0) of a symmetric tensor."""
+        h = self.symm.rendezvous(t, self.group.group_name)
+        base = h.buffer_ptrs[self.rank]
+        off = t.data_ptr() - base
+        if off < 0 or off + t.numel() * t.element_size() > h.buffer_size:
+            raise RuntimeError("symmetric tensor outside its allocation")
+        mc = h.multicast_ptr + off if h.multicast_ptr else 0
+        return h, [p + off for p in h.buffer_ptrs], mc
+
+    MAX_TILES = 1 << 16   # 256 x 256 output tiles: up to 2^32 output elements
+
+    def _control(self, tiles):
+        """Per-tile counters and the completion counter, zeroed on every rank
+        before any rank can signal (a barrier follows the clear); each
+        successful call leaves them zero again."""
+        t = self.torch
+        if tiles > self.MAX_TILES:
+            raise ValueError("output too large for the fused all-reduce")
+        if self._ctrl is None:
+            dev = t.device("cuda", t.cuda.current_device())
+            flags = self.symm.empty(self.MAX_TILES, dtype=t.int32, device=dev)
+            done = self.symm.empty(64, dtype=t.int32, device=dev)
+            flags.zero_()
+            done.zero_()
+            t.cuda.synchronize()
+            hf, pf, _ = self._map(flags)
+            hd, pd, mcd = self._map(done)
+            self.dist.barrier(group=self.group)
+            self._ctrl = dict(flags=flags, done=done, handles=(hf, hd), peer_flags=pf, peer_done=pd, mc_done=mcd)
+        return self._ctrl
+
+    def buffers(self, m, n):
+        """(partial, out, nq_allreduce_desc_t) for an m x n bf16 output."""
+        key = (m, n)
+        if key not in self._shapes:
+            t, nq = self.torch, self.nq
+            dev = t.device("cuda", t.cuda.current_device())
+            ctrl = self._control(nq.gemm_allreduce_counters(m, n))
+            partial = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
+            out = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
+            hp, pp, mcp = self._map(partial)
+            ho, po, mco = self._map(out)
+            use_mc = self.mode == "nvls" or (self.mode == "auto" and mcp and mco and ctrl["mc_done"])
+            if use_mc and not (mcp and mco and ctrl["mc_done"]):
+                raise RuntimeError("NVSwitch multicast is not available for these buffers (mode 'nvls')")
+            d = nq.AllreduceDesc()
+            d.tp, d.rank = self.tp, self.rank
+            d.partial, d.out = partial.data_ptr(), out.data_ptr()
+            if use_mc:
+                d.mc_partial, d.mc_out, d.mc_done = mcp, mco, ctrl["mc_done"]
+            d.flags, d.done = ctrl["flags"].data_ptr(), ctrl["done"].data_ptr()
+            for r in range(self.tp):
+                d.peer_flags[r] = ctrl["peer_flags"][r]
+                d.peer_partial[r], d.peer_out[r], d.peer_done[r] = pp[r], po[r], ctrl["peer_done"][r]
+            # kept for the layer's lifetime: peers may still be reading a
+            # buffer when this rank moves on to another shape
+            self._shapes[key] = (partial, out, d, (hp, ho))
+        partial, out, d, _ = self._shapes[key]
+        return partial, out, d
+
+    @property
+    def multicast(self):
+        return any(v[2].mc_partial for v in self._shapes.values())
+
+
 # ---- layers ------------------------------------------------------------------------
 class _FP8Linear:
     """Per-channel FP8 E4M3 weight (K x N, row-major) on the current device,
@@ -189,11 +279,17 @@ class RowParallelLayer:
     [batch*seq x in_features/tp] this rank's shard, output [batch*seq x
     out_features] replicated after the sum all-reduce (bf16, chunked)."""
 
-    def __init__(self, in_features: int, out_features: int, group=None, chunks=None):
+    def __init__(self, in_features: int, out_features: int, group=None, chunks=None, allreduce: str = "auto"):
         import torch
+        if allreduce not in ("auto", "nvls", "p2p", "nccl"):
+            raise ValueError("allreduce must be 'auto', 'nvls', 'p2p' or 'nccl'")
         self.torch, self.group = torch, group
         self.rank, self.tp = _group_info(group)
         self.chunks = chunks if chunks is not None else (4 if self.tp > 1 else 1)
+        # fused: one kernel does the GEMM and the all-reduce over peer memory
+        # (nq_gemm_allreduce); nccl: GEMM chunks + torch.distributed all_reduce
+        self.allreduce = allreduce if self.tp > 1 else "none"
+        self.fused = SymmetricAllReduce(group, allreduce) if self.tp > 1 and allreduce != "nccl" else None
         if in_features % self.tp:
             raise ValueError("in_features must be divisible by the TP degree")
         self.in_features, self.out_features = in_features, out_features
@@ -204,14 +300,30 @@ class RowParallelLayer:
         self.torch.cuda.current_stream().synchronize()
 
     def forward(self, input, output, batch: int, seq: int, sync: bool = True):
+        """output None (fused all-reduce only): returns the layer's symmetric
+        output buffer, valid until the next forward of this shape."""
         T = batch * seq
         if self.lin.q is None:
             raise RuntimeError("RowParallelLayer: set_weight has not been called")
         _check_io(self.torch, input, T, self.in_features // self.tp, "input")
-        _check_io(self.torch, output, T, self.out_features, "output")
+        if output is not None or self.fused is None:
+            _check_io(self.torch, output, T, self.out_features, "output")
         if T == 0:
             return output
         xq, sx = self.lin.act(input, T)
+        if self.fused is not None:
+            _, out, ard = self.fused.buffers(T, self.out_features)
+            lin, nq = self.lin, self.lin.nq
+            d = nq.make_desc(T, lin.n, lin.k, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, sx.data_ptr(),
+                             lin.s.data_ptr(), 0)
+            nq.gemm_allreduce(d, ard, xq.data_ptr(), lin.q.data_ptr(), self.torch.cuda.current_stream().cuda_stream)
+            if output is None:
+                output = out
+            else:
+                output.copy_(out)
+            if sync:
+                self.torch.cuda.current_stream().synchronize()
+            return output
 
         def compute(r0, r1):
             self.lin.gemm(xq, sx, output, r0, r1)
@@ -234,7 +346,7 @@ class TensorParallelMLP:
     GEMM with the SwiGLU epilogue produces silu(g) * u directly."""
 
     def __init__(self, hidden_dim: int, intermediate_size: int, group=None, chunks=None,
-                 overlap: str = "full"):
+                 overlap: str = "full", allreduce: str = "auto"):
         import torch
         if overlap not in ("full", "down"):
             raise ValueError("overlap must be 'full' or 'down'")
@@ -250,7 +362,7 @@ class TensorParallelMLP:
         # all-reduce to overlap, else 1 (an explicit value is always honoured)
         self.chunks = chunks if chunks is not None else (4 if self.tp > 1 else 1)
         self.gate_up = _FP8Linear()
-        self.down = RowParallelLayer(intermediate_size, hidden_dim, group, self.chunks)
+        self.down = RowParallelLayer(intermediate_size, hidden_dim, group, self.chunks, allreduce)
         self._h = {}
 
     def set_weight(self, gate_weight, up_weight, down_weight):
@@ -275,7 +387,8 @@ class TensorParallelMLP:
         if self.gate_up.q is None:
             raise RuntimeError("TensorParallelMLP: set_weight has not been called")
         _check_io(t, input, T, self.H, "input")
-        _check_io(t, output, T, self.H, "output")
+        if output is not None or self.down.fused is None:
+            _check_io(t, output, T, self.H, "output")
         if T == 0:
             return output
         if T not in self._h:
@@ -284,6 +397,10 @@ class TensorParallelMLP:
         epi = self.gate_up.nq.EPI_SWIGLU
         down = self.down.lin
         xq, sx = self.gate_up.act(input, T)
+        if self.down.fused is not None:
+            # one gate/up GEMM, then the down GEMM with the all-reduce fused in
+            self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)
+            return self.down.forward(h, output, batch, seq, sync)
         bounds = chunk_bounds(T, self.chunks)
         if self.overlap == "down" or len(bounds) == 1:
             self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)

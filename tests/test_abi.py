@@ -49,6 +49,30 @@ def test_status_strings_and_errors_without_gpu():
     assert capi.lib.nq_fp8_gemm_workspace_size(128, 256, 128) == 128 * 256 + 256 * 128 + 128 * 128 * 4
 
 
+def test_gemm_allreduce_argument_checks_without_gpu():
+    """nq_gemm_allreduce validates its descriptors before touching a device."""
+    import ctypes as C
+    import nova_b200.capi as capi
+    assert capi.lib.nq_gemm_allreduce_counters(16384, 8192) == 64 * 32
+    assert capi.lib.nq_gemm_allreduce_counters(300, 512) == 2 * 2
+    assert capi.lib.nq_gemm_allreduce_counters(0, 512) == 0
+    d = capi.make_desc(256, 512, 256)
+    ar = capi.AllreduceDesc()
+    ar.tp, ar.rank = 2, 0
+    assert capi.gemm_allreduce.raw(None, C.byref(ar), 16, 16, None) == 1          # null descriptor
+    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 1    # no buffers
+    ar.partial, ar.out, ar.flags, ar.done = 256, 512, 1024, 2048
+    ar.tp = 9
+    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 1    # tp > NQ_MAX_TP
+    ar.tp = 2
+    d.n = 384
+    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 2    # n % 256 != 0: unsupported
+    d.n, d.out_dtype = 512, capi.F32
+    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 2    # bf16 output only
+    d.out_dtype = capi.BF16
+    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 1    # peer pointers missing
+
+
 def test_no_device_is_an_error_not_a_crash():
     torch = pytest.importorskip("torch")
     if torch.cuda.is_available():

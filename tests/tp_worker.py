@@ -22,24 +22,35 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
     rank, world = dist.get_rank(), dist.get_world_size()
     ok = True
-    for T, H, I, overlap in [(600, 256, 512, "full"), (1024, 512, 1024, "down"), (1000, 512, 2048, "full")]:
-        x, wg, wu, wd = weights(T, H, I)
-        mlp = TensorParallelMLP(H, I, overlap=overlap)
-        mlp.set_weight(wg, wu, wd)
-        out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
-        mlp.forward(to_dev_bf16(x), out, 1, T)
-        # every rank holds the same replicated output
-        mx = out.float().clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        flag = torch.tensor([int(torch.equal(mx, out.float()))], device="cuda")
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        hs = [torch.empty_like(mlp._h[T]) for _ in range(world)]
-        dist.all_gather(hs, mlp._h[T])
-        if rank == 0:
-            h_err, out_err, full_err = check_mlp(bits(out), [bits(h) for h in hs], x, wg, wu, wd, world)
-            print(f"T={T} H={H} I={I} tp={world} overlap={overlap} chunks={mlp.chunks} h_err={h_err:.3e} "
-                  f"out_err={out_err:.3e} full_norm_err={full_err:.3e} replicated={bool(flag.item())}")
-            ok = ok and h_err <= 1e-2 and out_err <= 1e-2 and full_err <= 1e-2 and bool(flag.item())
+    modes = sys.argv[1:] or ["nccl", "p2p", "auto"]
+    cases = [(600, 256, 512, "full"), (1024, 512, 1024, "down"), (1000, 512, 2048, "full"), (600, 256, 512, "full")]
+    for allreduce in modes:
+        for T, H, I, overlap in cases:
+            x, wg, wu, wd = weights(T, H, I)
+            mlp = TensorParallelMLP(H, I, overlap=overlap, allreduce=allreduce)
+            mlp.set_weight(wg, wu, wd)
+            out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+            for _ in range(2):   # repeated calls: the fused path's counters must come back to zero
+                out.zero_()
+                mlp.forward(to_dev_bf16(x), out, 1, T)
+            # every rank holds the same replicated output
+            mx = out.float().clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            flag = torch.tensor([int(torch.equal(mx, out.float()))], device="cuda")
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            hs = [torch.empty_like(mlp._h[T]) for _ in range(world)]
+            dist.all_gather(hs, mlp._h[T])
+            import nova_b200.capi as nq
+            errs = torch.tensor([nq.device_error_flags()], device="cuda")
+            dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+            if rank == 0:
+                h_err, out_err, full_err = check_mlp(bits(out), [bits(h) for h in hs], x, wg, wu, wd, world)
+                mc = mlp.down.fused.multicast if mlp.down.fused is not None else False
+                print(f"allreduce={allreduce} multicast={mc} T={T} H={H} I={I} tp={world} overlap={overlap} "
+                      f"h_err={h_err:.3e} out_err={out_err:.3e} full_norm_err={full_err:.3e} "
+                      f"replicated={bool(flag.item())} device_errors={int(errs.item())}", flush=True)
+                ok = ok and h_err <= 1e-2 and out_err <= 1e-2 and full_err <= 1e-2 and bool(flag.item()) \
+                    and int(errs.item()) == 0
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
