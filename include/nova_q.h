@@ -229,16 +229,18 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  *     peer's `out`.
  * The kernel returns when this rank's `out` holds every tile, so `out` is
  * complete on the stream afterwards.  All buffers are symmetric allocations
- * (same size on every rank, mapped into every peer); `flags` (at least
- * nq_gemm_allreduce_counters(m, n) words) and `done` must be zero before the
- * first call and are left zero by every successful call.  Every rank must make
- * the same sequence of calls with the same m, n.  Waits on other GPUs give up
+ * (same size on every rank, mapped into every peer).  `flags` (at least
+ * nq_gemm_allreduce_counters(m, n) words) and `done` are counters that only
+ * grow: they must be zero before the call with epoch 1, and the n-th call on
+ * one set of buffers passes epoch n (so one set of buffers serves one m x n).
+ * Every rank makes the same sequence of calls.  Waits on other GPUs give up
  * after 5 s and set the device error word (nq_device_error_flags).
  * Requirements: desc->out_dtype NQ_BF16, desc->epilogue NQ_EPI_NONE,
  * n % 256 == 0, k % 16 == 0, 1 <= tp <= NQ_MAX_TP. */
 #define NQ_MAX_TP 8
 typedef struct {
     int tp, rank;
+    uint32_t epoch;      /* 1 for the first call on these buffers, then 2, 3, ... */
     void* partial;       /* this rank's M x N bf16 partial buffer */
     void* out;           /* this rank's M x N bf16 output buffer */
     void* mc_partial;    /* multicast address of the partial buffers, or NULL */

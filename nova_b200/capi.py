@@ -41,7 +41,7 @@ MAX_TP = 8
 
 
 class AllreduceDesc(C.Structure):
-    _fields_ = [("tp", C.c_int), ("rank", C.c_int), ("partial", C.c_void_p), ("out", C.c_void_p),
+    _fields_ = [("tp", C.c_int), ("rank", C.c_int), ("epoch", C.c_uint32), ("partial", C.c_void_p), ("out", C.c_void_p),
                 ("mc_partial", C.c_void_p), ("mc_out", C.c_void_p), ("mc_done", C.c_void_p),
                 ("flags", C.c_void_p), ("done", C.c_void_p),
                 ("peer_flags", C.c_void_p * MAX_TP), ("peer_partial", C.c_void_p * MAX_TP),

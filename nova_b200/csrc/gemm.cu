@@ -55,6 +55,7 @@ struct Epi {
 // Device view of nq_allreduce_desc_t: the all-reduce epilogue of k_gemm_tc2.
 struct ArParams {
     int tp, rank;
+    uint32_t epoch;
     uint8_t* mc_partial;
     uint8_t* mc_out;
     uint32_t* mc_done;
@@ -415,20 +416,25 @@ constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_SLOT;
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
 
 
-// Owner side of the fused all-reduce, run by one warp per cluster (warp 1 of
-// the pair's second CTA, idle in the GEMM).  For every tile this cluster
-// computes and this rank owns (tile % tp == rank): wait until all tp ranks'
-// 16 epilogue warps have stored their partial of the tile, sum the tp partials
-// (multicast: multimem.ld_reduce with fp32 accumulation in the switch; peer:
-// fp32 sum in rank order), write the bf16 sum to every rank's output, reset
-// the tile's counter and count the tile on every rank's completion counter.
-// Cluster 0 then waits until this rank's output holds all tiles.  32 lanes
-// cover the 512 bytes of one tile row; 8 (multicast) or 4 (peer) rows in flight.
-__device__ __forceinline__ void ar_reduce(const ArParams& ar, int cluster, int nclusters, int m_tiles, int n_tiles,
-                                          int M, int N, uint32_t* err) {
+// Owner side of the fused all-reduce, run by AR_WARPS reducer warps per
+// cluster (warps 10 and 11 of both CTAs and warp 1 of the second CTA, which
+// the GEMM leaves idle).  For every tile this cluster computes and this rank
+// owns (tile % tp == rank) every reducer warp waits until all tp ranks' 16
+// epilogue warps have stored their partial of the tile, then sums rows
+// j, j + AR_WARPS, ... of it over the ranks (multicast: multimem.ld_reduce with
+// fp32 accumulation in the switch; peer: fp32 sum in rank order), writes the
+// bf16 rows to every rank's output and counts itself on every rank's
+// completion counter.  Counters only grow: call `epoch` (1, 2, ...) waits for
+// epoch * (arrivals per call).  Reducer 0 of cluster 0 finally waits until
+// this rank's output holds every row of every tile.  32 lanes cover the 512
+// bytes of a tile row; 8 (multicast) or 4 (peer) rows in flight per warp.
+constexpr int AR_WARPS = 5;
+constexpr int P_THREADS_AR = P_THREADS + 64;  // + warps 10, 11
+__device__ __forceinline__ void ar_reduce(const ArParams& ar, int j, int cluster, int nclusters, int m_tiles,
+                                          int n_tiles, int M, int N, uint32_t* err) {
     const int lane = threadIdx.x & 31;
     const int num_tiles = m_tiles * n_tiles;
-    const uint32_t want = static_cast<uint32_t>(ar.tp) * (2 * P_EPI_WARPS);
+    const uint32_t want = ar.epoch * static_cast<uint32_t>(ar.tp) * (2 * P_EPI_WARPS);
     const size_t pitch = static_cast<size_t>(N) * 2;
     bool ok = true;
     for (int t = cluster; t < num_tiles; t += nclusters) {
@@ -442,31 +448,35 @@ __device__ __forceinline__ void ar_reduce(const ArParams& ar, int cluster, int n
         const int rows = min(P_BM, M - r0);
         const size_t base = static_cast<size_t>(r0) * pitch + static_cast<size_t>(nb) * P_BN * 2 + lane * 16;
         if (ar.mc_partial) {
-            for (int r = 0; r < rows; r += 8) {
-                uint4 v[8];
+            constexpr int U = 8;
+            for (int r = j; r < rows; r += U * AR_WARPS) {
+                uint4 v[U];
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    if (r + u < rows) v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u) * pitch);
+                for (int u = 0; u < U; ++u)
+                    if (r + u * AR_WARPS < rows)
+                        v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u * AR_WARPS) * pitch);
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    if (r + u < rows) multimem_st_v4(ar.mc_out + base + (r + u) * pitch, v[u]);
+                for (int u = 0; u < U; ++u)
+                    if (r + u * AR_WARPS < rows) multimem_st_v4(ar.mc_out + base + (r + u * AR_WARPS) * pitch, v[u]);
             }
         } else {
-            for (int r = 0; r < rows; r += 4) {
-                float acc[4][8];
+            constexpr int U = 4;
+            for (int r = j; r < rows; r += U * AR_WARPS) {
+                float acc[U][8];
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
+                for (int u = 0; u < U; ++u)
 #pragma unroll
                     for (int e = 0; e < 8; ++e) acc[u][e] = 0.0f;
                 for (int p = 0; p < ar.tp; ++p) {
-                    uint4 q[4];
+                    uint4 q[U];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        if (r + u < rows)
-                            q[u] = __ldcg(reinterpret_cast<const uint4*>(ar.peer_partial[p] + base + (r + u) * pitch));
+                    for (int u = 0; u < U; ++u)
+                        if (r + u * AR_WARPS < rows)
+                            q[u] = __ldcg(reinterpret_cast<const uint4*>(ar.peer_partial[p] + base +
+                                                                         (r + u * AR_WARPS) * pitch));
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        if (r + u >= rows) continue;
+                    for (int u = 0; u < U; ++u) {
+                        if (r + u * AR_WARPS >= rows) continue;
                         const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
@@ -476,17 +486,16 @@ __device__ __forceinline__ void ar_reduce(const ArParams& ar, int cluster, int n
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (r + u >= rows) continue;
+                for (int u = 0; u < U; ++u) {
+                    if (r + u * AR_WARPS >= rows) continue;
                     const uint4 o = make_uint4(f32x2_to_bf16x2(acc[u][0], acc[u][1]), f32x2_to_bf16x2(acc[u][2], acc[u][3]),
                                                f32x2_to_bf16x2(acc[u][4], acc[u][5]), f32x2_to_bf16x2(acc[u][6], acc[u][7]));
                     for (int p = 0; p < ar.tp; ++p)
-                        __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u) * pitch), o);
+                        __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u * AR_WARPS) * pitch), o);
                 }
             }
         }
-        // every arrival of this call is in: the counter is free for the next call
-        if (lane == 0) ar.flags[t] = 0u;
+        // this warp's rows are written everywhere: count them on every rank
         fence_acq_rel_sys();
         __syncwarp();
         if (lane == 0) {
@@ -495,13 +504,8 @@ __device__ __forceinline__ void ar_reduce(const ArParams& ar, int cluster, int n
                 for (int p = 0; p < ar.tp; ++p) red_add_release_sys(ar.peer_done[p], 1u);
         }
     }
-    if (cluster == 0 && lane == 0 && ok) {
-        // the last arrival of this call: the counter is free for the next call
-        if (wait_sys_geq(ar.done, static_cast<uint32_t>(num_tiles), err, kPeerWaitLimitNs)) {
-            *reinterpret_cast<volatile uint32_t*>(ar.done) = 0u;
-            fence_acq_rel_sys();
-        }
-    }
+    if (cluster == 0 && j == 0 && lane == 0 && ok)
+        wait_sys_geq(ar.done, ar.epoch * static_cast<uint32_t>(num_tiles) * AR_WARPS, err, kPeerWaitLimitNs);
 }
 
 // OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
@@ -511,7 +515,7 @@ __device__ __forceinline__ void ar_reduce(const ArParams& ar, int cluster, int n
 // AR: the partial tile goes to this rank's partial buffer (tmC) and the
 // tile's owner reduces it across ranks (ar_reduce); bf16 output only.
 template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU, bool AR>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
                const __grid_constant__ ArParams ar, uint32_t* err) {
@@ -595,8 +599,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA only) ----------------
         if constexpr (AR) {
-            // the second CTA's warp 1 reduces the tiles this rank owns
-            if (rank == 1) ar_reduce(ar, cluster, nclusters, m_tiles, n_tiles, M, N, err);
+            // the second CTA's warp 1 is one of the reducers
+            if (rank == 1) ar_reduce(ar, 2, cluster, nclusters, m_tiles, n_tiles, M, N, err);
         }
         if (rank == 0 && elect_one()) {
             int stage = 0;
@@ -634,6 +638,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             tc_commit_pair_mc(done, 0x1);
             mbar_wait(done, 0, err);
         }
+    } else if (AR && warp >= 2 + P_EPI_WARPS) {
+        // ---------------- all-reduce (warps 10, 11 of both CTAs) ----------------
+        const int j = warp - 2 - P_EPI_WARPS + (rank == 0 ? 0 : 3);
+        ar_reduce(ar, j, cluster, nclusters, m_tiles, n_tiles, M, N, err);
     } else {
         // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
         const int quarter = warp & 3;            // TMEM lanes [32 * quarter, +32)
@@ -1244,7 +1252,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     if (!max_clusters[di.device & 63]) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (di.sm_count / 2));
-        cfg.blockDim = dim3(P_THREADS);
+        cfg.blockDim = dim3(AR ? P_THREADS_AR : P_THREADS);
         cfg.dynamicSmemBytes = P_SMEM_BYTES;
         int nc = 0;
         if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess || nc <= 0) {
@@ -1255,6 +1263,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     }
     const int tiles = ((d.m + P_BM - 1) / P_BM) * ((d.n + P_BN - 1) / P_BN);
     const int clusters = std::max(1, std::min(tiles, max_clusters[di.device & 63]));
+    constexpr int threads = AR ? P_THREADS_AR : P_THREADS;
     const int grid = 2 * clusters;
     const int kblocks = (d.k + BK - 1) / BK;
     SplitTail tail{tiles, 0, 1, nullptr, nullptr};
@@ -1282,7 +1291,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     ArParams ar;
     if (arp) ar = *arp;
     else std::memset(&ar, 0, sizeof(ar));
-    kern<<<grid, P_THREADS, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, ar, err);
+    kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, ar, err);
     cudaError_t e = cudaGetLastError();
     if (scratch) scratch_free(scratch, s);
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
@@ -1449,8 +1458,8 @@ nq_status_t gemm_allreduce_impl(const nq_gemm_desc_t* d, const nq_allreduce_desc
         return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: bf16 output without a fused activation only");
     if (d->n % P_BN != 0 || d->k % 16 != 0 || !aligned16(a) || !aligned16(b))
         return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: needs n % 256 == 0, k % 16 == 0, 16-byte aligned operands");
-    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp)
-        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: tp / rank");
+    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp || r->epoch == 0)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: tp / rank / epoch");
     if (!r->partial || !r->out || !r->flags || !r->done || !aligned16(r->partial) || !aligned16(r->out))
         return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: partial / out / flags / done");
     const bool mc = r->mc_partial != nullptr;
@@ -1469,6 +1478,7 @@ nq_status_t gemm_allreduce_impl(const nq_gemm_desc_t* d, const nq_allreduce_desc
     std::memset(&ar, 0, sizeof(ar));
     ar.tp = r->tp;
     ar.rank = r->rank;
+    ar.epoch = r->epoch;
     ar.mc_partial = static_cast<uint8_t*>(r->mc_partial);
     ar.mc_out = static_cast<uint8_t*>(r->mc_out);
     ar.mc_done = r->mc_done;

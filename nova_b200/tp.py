@@ -122,7 +122,6 @@ class SymmetricAllReduce:
             raise ValueError(f"the fused all-reduce supports up to {capi.MAX_TP} ranks")
         self.mode = mode
         self._shapes = {}
-        self._ctrl = None
 
     def _map(self, t):
         """(local, [peer pointers], multicast pointer or 0) of a symmetric tensor."""
@@ -134,55 +133,45 @@ class SymmetricAllReduce:
         mc = h.multicast_ptr + off if h.multicast_ptr else 0
         return h, [p + off for p in h.buffer_ptrs], mc
 
-    MAX_TILES = 1 << 16   # 256 x 256 output tiles: up to 2^32 output elements
-
-    def _control(self, tiles):
-        """Per-tile counters and the completion counter, zeroed on every rank
-        before any rank can signal (a barrier follows the clear); each
-        successful call leaves them zero again."""
-        t = self.torch
-        if tiles > self.MAX_TILES:
-            raise ValueError("output too large for the fused all-reduce")
-        if self._ctrl is None:
+    def buffers(self, m, n):
+        """(partial, out, nq_allreduce_desc_t) for an m x n bf16 output, the
+        descriptor's epoch advanced for this call.  Each shape has its own
+        buffers and counters (zeroed on every rank before any rank can signal:
+        a barrier follows the clear); they live as long as the layer, since
+        peers may still be reading one when this rank moves to another shape."""
+        key = (m, n)
+        if key not in self._shapes:
+            t, nq = self.torch, self.nq
             dev = t.device("cuda", t.cuda.current_device())
-            flags = self.symm.empty(self.MAX_TILES, dtype=t.int32, device=dev)
-            done = self.symm.empty(64, dtype=t.int32, device=dev)
+            tiles = nq.gemm_allreduce_counters(m, n)
+            flags = self.symm.empty(tiles, dtype=t.int32, device=dev)
+            done = self.symm.empty(16, dtype=t.int32, device=dev)
+            partial = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
+            out = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
             flags.zero_()
             done.zero_()
             t.cuda.synchronize()
             hf, pf, _ = self._map(flags)
             hd, pd, mcd = self._map(done)
-            self.dist.barrier(group=self.group)
-            self._ctrl = dict(flags=flags, done=done, handles=(hf, hd), peer_flags=pf, peer_done=pd, mc_done=mcd)
-        return self._ctrl
-
-    def buffers(self, m, n):
-        """(partial, out, nq_allreduce_desc_t) for an m x n bf16 output."""
-        key = (m, n)
-        if key not in self._shapes:
-            t, nq = self.torch, self.nq
-            dev = t.device("cuda", t.cuda.current_device())
-            ctrl = self._control(nq.gemm_allreduce_counters(m, n))
-            partial = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
-            out = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
             hp, pp, mcp = self._map(partial)
             ho, po, mco = self._map(out)
-            use_mc = self.mode == "nvls" or (self.mode == "auto" and mcp and mco and ctrl["mc_done"])
-            if use_mc and not (mcp and mco and ctrl["mc_done"]):
+            self.dist.barrier(group=self.group)
+            have_mc = bool(mcp and mco and mcd)
+            use_mc = self.mode == "nvls" or (self.mode == "auto" and have_mc)
+            if use_mc and not have_mc:
                 raise RuntimeError("NVSwitch multicast is not available for these buffers (mode 'nvls')")
             d = nq.AllreduceDesc()
-            d.tp, d.rank = self.tp, self.rank
+            d.tp, d.rank, d.epoch = self.tp, self.rank, 0
             d.partial, d.out = partial.data_ptr(), out.data_ptr()
             if use_mc:
-                d.mc_partial, d.mc_out, d.mc_done = mcp, mco, ctrl["mc_done"]
-            d.flags, d.done = ctrl["flags"].data_ptr(), ctrl["done"].data_ptr()
+                d.mc_partial, d.mc_out, d.mc_done = mcp, mco, mcd
+            d.flags, d.done = flags.data_ptr(), done.data_ptr()
             for r in range(self.tp):
-                d.peer_flags[r] = ctrl["peer_flags"][r]
-                d.peer_partial[r], d.peer_out[r], d.peer_done[r] = pp[r], po[r], ctrl["peer_done"][r]
-            # kept for the layer's lifetime: peers may still be reading a
-            # buffer when this rank moves on to another shape
-            self._shapes[key] = (partial, out, d, (hp, ho))
+                d.peer_flags[r], d.peer_done[r] = pf[r], pd[r]
+                d.peer_partial[r], d.peer_out[r] = pp[r], po[r]
+            self._shapes[key] = (partial, out, d, (flags, done, hf, hd, hp, ho))
         partial, out, d, _ = self._shapes[key]
+        d.epoch += 1
         return partial, out, d
 
     @property
