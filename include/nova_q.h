@@ -219,7 +219,8 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  * tensor_parallel_layers.cpp:370-416: a GEMM on the rank's K shard, then
  * ncclAllReduce(sum) of the M x N output, :406) as ONE kernel per rank.  Every
  * rank writes its bf16 partial tile to its `partial` buffer and raises the
- * tile's counter on the tile's owner (rank = tile % tp).  Inside the same
+ * tile's counter on the tile's owner (ownership rotates over the ranks, 1/tp
+ * of the tiles each).  Inside the same
  * kernel the owner's reducer warps wait for all tp partials of each owned
  * tile, sum them and write the sum to every rank's `out`:
  *   multicast (mc_partial/mc_out/mc_done non-NULL): multimem.ld_reduce

@@ -419,7 +419,7 @@ constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_B
 // Owner side of the fused all-reduce, run by AR_WARPS reducer warps per
 // cluster (warps 10 and 11 of both CTAs and warp 1 of the second CTA, which
 // the GEMM leaves idle).  For every tile this cluster computes and this rank
-// owns (tile % tp == rank) every reducer warp waits until all tp ranks' 16
+// owns (ar_owner) every reducer warp waits until all tp ranks' 16
 // epilogue warps have stored their partial of the tile, then sums rows
 // j, j + AR_WARPS, ... of it over the ranks (multicast: multimem.ld_reduce with
 // fp32 accumulation in the switch; peer: fp32 sum in rank order), writes the
@@ -427,9 +427,16 @@ constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_B
 // completion counter.  Counters only grow: call `epoch` (1, 2, ...) waits for
 // epoch * (arrivals per call).  Reducer 0 of cluster 0 finally waits until
 // this rank's output holds every row of every tile.  32 lanes cover the 512
-// bytes of a tile row; 8 (multicast) or 4 (peer) rows in flight per warp.
+// bytes of a tile row; 10 (multicast) or 4 (peer) rows in flight per warp.
 constexpr int AR_WARPS = 5;
 constexpr int P_THREADS_AR = P_THREADS + 64;  // + warps 10, 11
+// Owner rank of a tile: cluster c computes tiles c, c + nclusters, ... (wave
+// k = tile / nclusters); ownership rotates over ranks along the clusters of a
+// wave and along the waves of a cluster, so every cluster's reducers get every
+// tp-th of its tiles and every rank owns 1/tp of each wave.
+__device__ __forceinline__ int ar_owner(int tile, int nclusters, int tp) {
+    return (tile / nclusters + tile % nclusters) % tp;
+}
 __device__ __forceinline__ void ar_reduce(const ArParams& ar, int j, int cluster, int nclusters, int m_tiles,
                                           int n_tiles, int M, int N, uint32_t* err) {
     const int lane = threadIdx.x & 31;
@@ -438,7 +445,7 @@ __device__ __forceinline__ void ar_reduce(const ArParams& ar, int j, int cluster
     const size_t pitch = static_cast<size_t>(N) * 2;
     bool ok = true;
     for (int t = cluster; t < num_tiles; t += nclusters) {
-        if (t % ar.tp != ar.rank) continue;
+        if (ar_owner(t, nclusters, ar.tp) != ar.rank) continue;
         if (lane == 0) ok = wait_sys_geq(ar.flags + t, want, err, kPeerWaitLimitNs);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
@@ -448,7 +455,7 @@ __device__ __forceinline__ void ar_reduce(const ArParams& ar, int j, int cluster
         const int rows = min(P_BM, M - r0);
         const size_t base = static_cast<size_t>(r0) * pitch + static_cast<size_t>(nb) * P_BN * 2 + lane * 16;
         if (ar.mc_partial) {
-            constexpr int U = 8;
+            constexpr int U = 10;
             for (int r = j; r < rows; r += U * AR_WARPS) {
                 uint4 v[U];
 #pragma unroll
@@ -865,7 +872,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 if (lane == 0) {
                     bulk_wait_group_all();
                     fence_proxy_async_global();
-                    red_add_release_sys(ar.peer_flags[tile % ar.tp] + tile, 1u);
+                    red_add_release_sys(ar.peer_flags[ar_owner(tile, nclusters, ar.tp)] + tile, 1u);
                 }
                 __syncwarp();
             }

@@ -26,6 +26,8 @@ def main():
     cases = [(600, 256, 512, "full"), (1024, 512, 1024, "down"), (1000, 512, 2048, "full"), (600, 256, 512, "full")]
     for allreduce in modes:
         for T, H, I, overlap in cases:
+            unit = 128 * world
+            I = max(unit, (I + unit - 1) // unit * unit)   # each rank's shard a multiple of 128
             x, wg, wu, wd = weights(T, H, I)
             mlp = TensorParallelMLP(H, I, overlap=overlap, allreduce=allreduce)
             mlp.set_weight(wg, wu, wd)
