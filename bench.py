@@ -421,7 +421,7 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4,
     fp8_peak = 2.0 * pk["bf16_tflops"]
     tflops = flops / (ms * 1e-3) / 1e12
     res = {"workload": "tp_fp8_swiglu_mlp (BASELINE configs[4])", "tokens": T, "hidden": H, "intermediate": I,
-           "tp": world, "allreduce": (("fused-nvls" if mlp.down.fused.multicast else "fused-p2p") if fused
+           "tp": world, "allreduce": (("fused-nvls" if mlp.down.fused.multicast() else "fused-p2p") if fused
                                       else ("nccl" if world > 1 else "none")),
            "chunks": chunks if not fused else 1, "overlap": overlap, "ms_per_step": round(ms, 4),
            "tokens_per_s": T / (ms * 1e-3), "tflops_total": tflops,

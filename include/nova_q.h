@@ -214,51 +214,73 @@ nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, vo
 nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out,
                          nq_stream_t s);
 
-/* ---- GEMM fused with the all-reduce of a row-parallel layer ------------------
- * The down projection of a tensor-parallel MLP (RowParallelLayer::forward,
- * tensor_parallel_layers.cpp:370-416: a GEMM on the rank's K shard, then
- * ncclAllReduce(sum) of the M x N output, :406) as ONE kernel per rank.  Every
- * rank writes its bf16 partial tile to its `partial` buffer and raises the
- * tile's counter on the tile's owner (ownership rotates over the ranks, 1/tp
- * of the tiles each).  Inside the same
- * kernel the owner's reducer warps wait for all tp partials of each owned
- * tile, sum them and write the sum to every rank's `out`:
- *   multicast (mc_partial/mc_out/mc_done non-NULL): multimem.ld_reduce
- *     (fp32 accumulation in the NVSwitch, one bf16 rounding) and multimem.st;
- *   peer (multicast NULL): loads of the tp partials through the peer
- *     pointers, fp32 sum in rank order, one bf16 rounding, stores to each
- *     peer's `out`.
- * The kernel returns when this rank's `out` holds every tile, so `out` is
- * complete on the stream afterwards.  All buffers are symmetric allocations
- * (same size on every rank, mapped into every peer).  `flags` (at least
- * nq_gemm_allreduce_counters(m, n) words) and `done` are counters that only
- * grow: they must be zero before the call with epoch 1, and the n-th call on
- * one set of buffers passes epoch n (so one set of buffers serves one m x n).
- * Every rank makes the same sequence of calls.  Waits on other GPUs give up
- * after 5 s and set the device error word (nq_device_error_flags).
- * Requirements: desc->out_dtype NQ_BF16, desc->epilogue NQ_EPI_NONE,
- * n % 256 == 0, k % 16 == 0, 1 <= tp <= NQ_MAX_TP. */
+/* ---- GEMMs fused with the all-reduce of a row-parallel layer ------------------
+ * RowParallelLayer::forward (tensor_parallel_layers.cpp:370-416) is a GEMM on
+ * the rank's K shard followed by ncclAllReduce(sum) of the M x N output
+ * (:406).  Here the all-reduce runs inside the GEMM kernels, over NVLink:
+ *
+ *  signal  the GEMM's output is a partial: its bf16 tiles go to the `out`
+ *          argument (this rank's partial buffer) and every epilogue warp adds
+ *          1 (16 per 256 x 256 tile) to the tile's counter on the tile's
+ *          owner rank (tile % tp);
+ *  job     the kernel's reducer warps (5 per CTA pair, beside the GEMM's own
+ *          warps) sum the tiles of an m x n output that this rank owns, once
+ *          all tp ranks have signalled them, and write the bf16 sum to every
+ *          rank's output buffer:
+ *            multicast (mc_partial / mc_out / mc_done non-NULL):
+ *              multimem.ld_reduce (fp32 accumulation in the NVSwitch, one bf16
+ *              rounding) and multimem.st;
+ *            peer (multicast NULL): loads of the tp partials through the
+ *              peer pointers, fp32 sum in rank order, one bf16 rounding,
+ *              stores to every peer;
+ *          each reducer warp then counts itself on every rank's completion
+ *          counter (5 counts per tile);
+ *  finish  with done_target > 0 the kernel returns only once this rank's
+ *          completion counter reaches done_target (its output buffer holds
+ *          every reduced tile).
+ *
+ * nq_gemm_allreduce runs a GEMM with any of the three; with all three on the
+ * GEMM's own output it is the whole row-parallel layer in one kernel.  A job
+ * on an EARLIER output lets a token chunk's all-reduce overlap the next
+ * chunk's GEMMs (the SwiGLU gate/up GEMM included).  nq_allreduce_finish runs
+ * a job and / or finish without a GEMM.
+ *
+ * All buffers are symmetric allocations (same size on every rank, mapped into
+ * every peer); job pointers address the job's first row.  Counters only
+ * grow: zero before epoch 1; the n-th use of a counter set passes epoch n and
+ * a job waits for its tiles' counters to reach epoch * tp * 16.  Every rank
+ * makes the same sequence of calls.  Waits on other GPUs give up after 5 s
+ * and set the device error word (nq_device_error_flags).  A signalling GEMM
+ * needs out_dtype NQ_BF16, epilogue NQ_EPI_NONE, n % 256 == 0; jobs need
+ * n % 256 == 0; 1 <= tp <= NQ_MAX_TP. */
 #define NQ_MAX_TP 8
 typedef struct {
     int tp, rank;
-    uint32_t epoch;      /* 1 for the first call on these buffers, then 2, 3, ... */
-    void* partial;       /* this rank's M x N bf16 partial buffer */
-    void* out;           /* this rank's M x N bf16 output buffer */
-    void* mc_partial;    /* multicast address of the partial buffers, or NULL */
-    void* mc_out;        /* multicast address of the output buffers, or NULL */
-    uint32_t* mc_done;   /* multicast address of the completion counters, or NULL */
-    uint32_t* flags;     /* this rank's per-tile arrival counters */
-    uint32_t* done;      /* this rank's completion counter */
-    uint32_t* peer_flags[NQ_MAX_TP];   /* every rank's `flags` (this rank's included) */
-    void* peer_partial[NQ_MAX_TP];     /* peer path: every rank's `partial` */
-    void* peer_out[NQ_MAX_TP];         /* peer path: every rank's `out` */
-    uint32_t* peer_done[NQ_MAX_TP];    /* peer path: every rank's `done` */
+    uint32_t epoch;                      /* 1 for the first use of the counters, then 2, ... */
+    /* signal */
+    int signal;                          /* 1: the GEMM's output is a partial */
+    uint32_t* signal_flags[NQ_MAX_TP];   /* every rank's counters of the output's tiles */
+    /* job */
+    int m, n;                            /* the output to reduce; m == 0: no job */
+    uint32_t* flags;                     /* this rank's counters of the job's tiles */
+    void* mc_partial;                    /* multicast partial buffers, or NULL */
+    void* mc_out;                        /* multicast output buffers, or NULL */
+    uint32_t* mc_done;                   /* multicast completion counters, or NULL */
+    void* peer_partial[NQ_MAX_TP];       /* peer path: every rank's partial buffer */
+    void* peer_out[NQ_MAX_TP];           /* peer path: every rank's output buffer */
+    uint32_t* peer_done[NQ_MAX_TP];      /* peer path: every rank's completion counter */
+    /* finish */
+    uint32_t* done;                      /* this rank's completion counter */
+    uint32_t done_target;                /* > 0: wait until *done >= done_target */
 } nq_allreduce_desc_t;
 
-/* Per-tile counters nq_gemm_allreduce needs for an m x n output. */
+/* Tiles (counters) of an m x n output. */
 int nq_gemm_allreduce_counters(int m, int n);
+/* Completion counts one job of an m x n output adds on every rank. */
+int nq_allreduce_done_per_job(int m, int n);
 nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* desc, const nq_allreduce_desc_t* ar,
-                              const void* a, const void* b, nq_stream_t s);
+                              const void* a, const void* b, void* out, nq_stream_t s);
+nq_status_t nq_allreduce_finish(const nq_allreduce_desc_t* ar, nq_stream_t s);
 
 /* FP8GEMM::forward / forward_async, include/cuda/quantize/fp8_gemm.hpp:55-69
    (fp8_gemm.cu:164-198): fp32 out = scale_out * sum (a*scale_a)(b*scale_b),

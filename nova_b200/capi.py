@@ -41,11 +41,13 @@ MAX_TP = 8
 
 
 class AllreduceDesc(C.Structure):
-    _fields_ = [("tp", C.c_int), ("rank", C.c_int), ("epoch", C.c_uint32), ("partial", C.c_void_p), ("out", C.c_void_p),
+    _fields_ = [("tp", C.c_int), ("rank", C.c_int), ("epoch", C.c_uint32),
+                ("signal", C.c_int), ("signal_flags", C.c_void_p * MAX_TP),
+                ("m", C.c_int), ("n", C.c_int), ("flags", C.c_void_p),
                 ("mc_partial", C.c_void_p), ("mc_out", C.c_void_p), ("mc_done", C.c_void_p),
-                ("flags", C.c_void_p), ("done", C.c_void_p),
-                ("peer_flags", C.c_void_p * MAX_TP), ("peer_partial", C.c_void_p * MAX_TP),
-                ("peer_out", C.c_void_p * MAX_TP), ("peer_done", C.c_void_p * MAX_TP)]
+                ("peer_partial", C.c_void_p * MAX_TP), ("peer_out", C.c_void_p * MAX_TP),
+                ("peer_done", C.c_void_p * MAX_TP),
+                ("done", C.c_void_p), ("done_target", C.c_uint32)]
 
 
 _SIGS = {
@@ -72,7 +74,8 @@ _SIGS = {
     "nq_quantize_cols_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "nq_gemm": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_gemm_simt": [C.POINTER(GemmDesc), _p, _p, _p, _p],
-    "nq_gemm_allreduce": [C.POINTER(GemmDesc), C.POINTER(AllreduceDesc), _p, _p, _p],
+    "nq_gemm_allreduce": [C.POINTER(GemmDesc), C.POINTER(AllreduceDesc), _p, _p, _p, _p],
+    "nq_allreduce_finish": [C.POINTER(AllreduceDesc), _p],
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_fp8e5m2_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_device_error_flags": [_u32p, _i],
@@ -89,6 +92,9 @@ lib.nq_fp8_gemm_workspace_size.argtypes = [_i, _i, _i]
 lib.nq_gemm_allreduce_counters.restype = C.c_int
 lib.nq_gemm_allreduce_counters.argtypes = [_i, _i]
 gemm_allreduce_counters = lib.nq_gemm_allreduce_counters
+lib.nq_allreduce_done_per_job.restype = C.c_int
+lib.nq_allreduce_done_per_job.argtypes = [_i, _i]
+allreduce_done_per_job = lib.nq_allreduce_done_per_job
 
 
 def _wrap(name, argtypes):
@@ -114,7 +120,7 @@ for _n, _a in _SIGS.items():
 
 def exported_symbols():
     return sorted(list(_SIGS) + ["nq_status_string", "nq_last_error", "nq_version", "nq_fp8_gemm_workspace_size",
-                                 "nq_gemm_allreduce_counters"])
+                                 "nq_gemm_allreduce_counters", "nq_allreduce_done_per_job"])
 
 
 EPI_NONE, EPI_SWIGLU = 0, 1

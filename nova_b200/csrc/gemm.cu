@@ -52,19 +52,23 @@ struct Epi {
     const float* bias;
 };
 
-// Device view of nq_allreduce_desc_t: the all-reduce epilogue of k_gemm_tc2.
+// Device view of nq_allreduce_desc_t (signal / job / finish of the fused
+// all-reduce; pointers as bytes).
 struct ArParams {
     int tp, rank;
     uint32_t epoch;
+    int signal;
+    uint32_t* signal_flags[NQ_MAX_TP];
+    int m, n;  // job; m == 0: none
+    uint32_t* flags;
     uint8_t* mc_partial;
     uint8_t* mc_out;
     uint32_t* mc_done;
-    uint32_t* flags;
-    uint32_t* done;
-    uint32_t* peer_flags[NQ_MAX_TP];
     const uint8_t* peer_partial[NQ_MAX_TP];
     uint8_t* peer_out[NQ_MAX_TP];
     uint32_t* peer_done[NQ_MAX_TP];
+    uint32_t* done;
+    uint32_t done_target;
 };
 // Upper bound of a wait on another GPU (its kernel may start a little later).
 constexpr uint64_t kPeerWaitLimitNs = 5000000000ull;
@@ -416,117 +420,119 @@ constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_SLOT;
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
 
 
-// Owner side of the fused all-reduce, run by AR_WARPS reducer warps per
-// cluster (warps 10 and 11 of both CTAs and warp 1 of the second CTA, which
-// the GEMM leaves idle).  For every tile this cluster computes and this rank
-// owns (ar_owner) every reducer warp waits until all tp ranks' 16
-// epilogue warps have stored their partial of the tile, then sums rows
-// j, j + AR_WARPS, ... of it over the ranks (multicast: multimem.ld_reduce with
-// fp32 accumulation in the switch; peer: fp32 sum in rank order), writes the
-// bf16 rows to every rank's output and counts itself on every rank's
-// completion counter.  Counters only grow: call `epoch` (1, 2, ...) waits for
-// epoch * (arrivals per call).  Reducer 0 of cluster 0 finally waits until
-// this rank's output holds every row of every tile.  32 lanes cover the 512
-// bytes of a tile row; 10 (multicast) or 4 (peer) rows in flight per warp.
+// Reducer side of the fused all-reduce.  A group of AR_WARPS warps (warps 10
+// and 11 of both CTAs of a GEMM pair plus the second CTA's idle warp 1, or
+// one CTA of the finish kernel) takes the owned tiles i = group, group +
+// ngroups, ... of the job (owned tile i is tile rank + tp * i in the producing
+// GEMM's tile order); warp j of the group waits until all tp ranks' 16
+// epilogue warps have signalled the tile, then sums its rows j, j + AR_WARPS,
+// ... over the ranks (multicast: multimem.ld_reduce, fp32 accumulation in the
+// switch; peer: fp32 sum in rank order) and writes the bf16 rows to every
+// rank's output, then counts itself on every rank's completion counter.
+// 32 lanes cover the 512 bytes of a tile row; 10 (multicast) or 4 (peer)
+// rows in flight per warp.  Finally warp 0 of group 0 waits for done_target.
 constexpr int AR_WARPS = 5;
 constexpr int P_THREADS_AR = P_THREADS + 64;  // + warps 10, 11
-// Owner rank of a tile: cluster c computes tiles c, c + nclusters, ... (wave
-// k = tile / nclusters); ownership rotates over ranks along the clusters of a
-// wave and along the waves of a cluster, so every cluster's reducers get every
-// tp-th of its tiles and every rank owns 1/tp of each wave.
-__device__ __forceinline__ int ar_owner(int tile, int nclusters, int tp) {
-    return (tile / nclusters + tile % nclusters) % tp;
-}
-__device__ __forceinline__ void ar_reduce(const ArParams& ar, int j, int cluster, int nclusters, int m_tiles,
-                                          int n_tiles, int M, int N, uint32_t* err) {
+constexpr int AR_SIGNALS_PER_TILE = 2 * P_EPI_WARPS;
+__device__ __forceinline__ void ar_job(const ArParams& ar, int j, int group, int ngroups, uint32_t* err) {
     const int lane = threadIdx.x & 31;
-    const int num_tiles = m_tiles * n_tiles;
-    const uint32_t want = ar.epoch * static_cast<uint32_t>(ar.tp) * (2 * P_EPI_WARPS);
-    const size_t pitch = static_cast<size_t>(N) * 2;
     bool ok = true;
-    for (int t = cluster; t < num_tiles; t += nclusters) {
-        if (ar_owner(t, nclusters, ar.tp) != ar.rank) continue;
-        if (lane == 0) ok = wait_sys_geq(ar.flags + t, want, err, kPeerWaitLimitNs);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        int mb, nb;
-        tile_coords(t, m_tiles, n_tiles, mb, nb);
-        const int r0 = mb * P_BM;
-        const int rows = min(P_BM, M - r0);
-        const size_t base = static_cast<size_t>(r0) * pitch + static_cast<size_t>(nb) * P_BN * 2 + lane * 16;
-        if (ar.mc_partial) {
-            constexpr int U = 10;
-            for (int r = j; r < rows; r += U * AR_WARPS) {
-                uint4 v[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (r + u * AR_WARPS < rows)
-                        v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u * AR_WARPS) * pitch);
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (r + u * AR_WARPS < rows) multimem_st_v4(ar.mc_out + base + (r + u * AR_WARPS) * pitch, v[u]);
-            }
-        } else {
-            constexpr int U = 4;
-            for (int r = j; r < rows; r += U * AR_WARPS) {
-                float acc[U][8];
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[u][e] = 0.0f;
-                for (int p = 0; p < ar.tp; ++p) {
-                    uint4 q[U];
+    if (ar.m > 0) {
+        const int m_tiles = (ar.m + P_BM - 1) / P_BM;
+        const int n_tiles = ar.n / P_BN;
+        const int num_tiles = m_tiles * n_tiles;
+        const uint32_t want = ar.epoch * static_cast<uint32_t>(ar.tp) * AR_SIGNALS_PER_TILE;
+        const size_t pitch = static_cast<size_t>(ar.n) * 2;
+        for (int i = group;; i += ngroups) {
+            const int t = ar.rank + ar.tp * i;
+            if (t >= num_tiles) break;
+            if (lane == 0) ok = wait_sys_geq(ar.flags + t, want, err, kPeerWaitLimitNs);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            int mb, nb;
+            tile_coords(t, m_tiles, n_tiles, mb, nb);
+            const int r0 = mb * P_BM;
+            const int rows = min(P_BM, ar.m - r0);
+            const size_t base = static_cast<size_t>(r0) * pitch + static_cast<size_t>(nb) * P_BN * 2 + lane * 16;
+            if (ar.mc_partial) {
+                constexpr int U = 10;
+                for (int r = j; r < rows; r += U * AR_WARPS) {
+                    uint4 v[U];
 #pragma unroll
                     for (int u = 0; u < U; ++u)
                         if (r + u * AR_WARPS < rows)
-                            q[u] = __ldcg(reinterpret_cast<const uint4*>(ar.peer_partial[p] + base +
-                                                                         (r + u * AR_WARPS) * pitch));
+                            v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u * AR_WARPS) * pitch);
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+                        if (r + u * AR_WARPS < rows) multimem_st_v4(ar.mc_out + base + (r + u * AR_WARPS) * pitch, v[u]);
+                }
+            } else {
+                constexpr int U = 4;
+                for (int r = j; r < rows; r += U * AR_WARPS) {
+                    float acc[U][8];
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[u][e] = 0.0f;
+                    for (int p = 0; p < ar.tp; ++p) {
+                        uint4 q[U];
+#pragma unroll
+                        for (int u = 0; u < U; ++u)
+                            if (r + u * AR_WARPS < rows)
+                                q[u] = __ldcg(reinterpret_cast<const uint4*>(ar.peer_partial[p] + base +
+                                                                             (r + u * AR_WARPS) * pitch));
+#pragma unroll
+                        for (int u = 0; u < U; ++u) {
+                            if (r + u * AR_WARPS >= rows) continue;
+                            const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                acc[u][2 * e] = __fadd_rn(acc[u][2 * e], __uint_as_float(w[e] << 16));
+                                acc[u][2 * e + 1] = __fadd_rn(acc[u][2 * e + 1], __uint_as_float(w[e] & 0xFFFF0000u));
+                            }
+                        }
+                    }
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
                         if (r + u * AR_WARPS >= rows) continue;
-                        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            acc[u][2 * e] = __fadd_rn(acc[u][2 * e], __uint_as_float(w[e] << 16));
-                            acc[u][2 * e + 1] = __fadd_rn(acc[u][2 * e + 1], __uint_as_float(w[e] & 0xFFFF0000u));
-                        }
+                        const uint4 o = make_uint4(f32x2_to_bf16x2(acc[u][0], acc[u][1]), f32x2_to_bf16x2(acc[u][2], acc[u][3]),
+                                                   f32x2_to_bf16x2(acc[u][4], acc[u][5]), f32x2_to_bf16x2(acc[u][6], acc[u][7]));
+                        for (int p = 0; p < ar.tp; ++p)
+                            __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u * AR_WARPS) * pitch), o);
                     }
                 }
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if (r + u * AR_WARPS >= rows) continue;
-                    const uint4 o = make_uint4(f32x2_to_bf16x2(acc[u][0], acc[u][1]), f32x2_to_bf16x2(acc[u][2], acc[u][3]),
-                                               f32x2_to_bf16x2(acc[u][4], acc[u][5]), f32x2_to_bf16x2(acc[u][6], acc[u][7]));
-                    for (int p = 0; p < ar.tp; ++p)
-                        __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u * AR_WARPS) * pitch), o);
-                }
+            }
+            // this warp's rows are written everywhere: count them on every rank
+            fence_acq_rel_sys();
+            __syncwarp();
+            if (lane == 0) {
+                if (ar.mc_done) multimem_red_add_release(ar.mc_done, 1u);
+                else
+                    for (int p = 0; p < ar.tp; ++p) red_add_release_sys(ar.peer_done[p], 1u);
             }
         }
-        // this warp's rows are written everywhere: count them on every rank
-        fence_acq_rel_sys();
-        __syncwarp();
-        if (lane == 0) {
-            if (ar.mc_done) multimem_red_add_release(ar.mc_done, 1u);
-            else
-                for (int p = 0; p < ar.tp; ++p) red_add_release_sys(ar.peer_done[p], 1u);
-        }
     }
-    if (cluster == 0 && j == 0 && lane == 0 && ok)
-        wait_sys_geq(ar.done, ar.epoch * static_cast<uint32_t>(num_tiles) * AR_WARPS, err, kPeerWaitLimitNs);
+    if (ar.done_target && group == 0 && j == 0 && lane == 0 && ok)
+        wait_sys_geq(ar.done, ar.done_target, err, kPeerWaitLimitNs);
+}
+
+// Job and / or finish without a GEMM: one CTA of AR_WARPS warps per group.
+__global__ void __launch_bounds__(AR_WARPS * 32) k_ar_finish(const __grid_constant__ ArParams ar, uint32_t* err) {
+    ar_job(ar, threadIdx.x >> 5, blockIdx.x, gridDim.x, err);
 }
 
 // OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
 // 1 = bf16 through TMA stores, 2 = int8 requantized, direct stores.
 // SWIGLU: columns [0,128) of each 256-wide tile are gate, [128,256) up; the
 // tile writes 128 columns of silu(g) * u.
-// AR: the partial tile goes to this rank's partial buffer (tmC) and the
-// tile's owner reduces it across ranks (ar_reduce); bf16 output only.
+// AR: the kernel carries the reducer warps of the fused all-reduce (ar_job)
+// and, with ar.signal, counts each bf16 output tile on its owner rank.
 template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU, bool AR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
                const __grid_constant__ ArParams ar, uint32_t* err) {
-    static_assert(!AR || (OUTK == 1 && !SWIGLU), "the all-reduce epilogue writes bf16 tiles");
+    static_assert(!AR || OUTK == 1, "the all-reduce signals bf16 tiles");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -607,7 +613,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         // ---------------- MMA issuer (leader CTA only) ----------------
         if constexpr (AR) {
             // the second CTA's warp 1 is one of the reducers
-            if (rank == 1) ar_reduce(ar, 2, cluster, nclusters, m_tiles, n_tiles, M, N, err);
+            if (rank == 1) ar_job(ar, 2, cluster, nclusters, err);
         }
         if (rank == 0 && elect_one()) {
             int stage = 0;
@@ -648,7 +654,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     } else if (AR && warp >= 2 + P_EPI_WARPS) {
         // ---------------- all-reduce (warps 10, 11 of both CTAs) ----------------
         const int j = warp - 2 - P_EPI_WARPS + (rank == 0 ? 0 : 3);
-        ar_reduce(ar, j, cluster, nclusters, m_tiles, n_tiles, M, N, err);
+        ar_job(ar, j, cluster, nclusters, err);
     } else {
         // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
         const int quarter = warp & 3;            // TMEM lanes [32 * quarter, +32)
@@ -868,13 +874,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 ++chunk_seq;
             }
             if constexpr (AR) {
-                // this warp's part of the partial tile is in memory: count it on the owner
-                if (lane == 0) {
-                    bulk_wait_group_all();
-                    fence_proxy_async_global();
-                    red_add_release_sys(ar.peer_flags[ar_owner(tile, nclusters, ar.tp)] + tile, 1u);
+                if (ar.signal) {
+                    // this warp's part of the partial tile is in memory: count it on the owner
+                    if (lane == 0) {
+                        bulk_wait_group_all();
+                        fence_proxy_async_global();
+                        red_add_release_sys(ar.signal_flags[tile % ar.tp] + tile, 1u);
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
         }
         if (lane == 0) bulk_wait_group_all();
@@ -1451,58 +1459,108 @@ nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, voi
     return NQ_SUCCESS;
 }
 
+namespace {
+nq_status_t fill_ar(const nq_allreduce_desc_t* r, ArParams* ar) {
+    std::memset(ar, 0, sizeof(*ar));
+    if (!r) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: null descriptor");
+    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp || r->epoch == 0)
+        return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: tp / rank / epoch");
+    ar->tp = r->tp;
+    ar->rank = r->rank;
+    ar->epoch = r->epoch;
+    ar->signal = r->signal ? 1 : 0;
+    if (ar->signal)
+        for (int p = 0; p < r->tp; ++p) {
+            if (!r->signal_flags[p]) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: signal_flags");
+            ar->signal_flags[p] = r->signal_flags[p];
+        }
+    if (r->m < 0) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: job rows");
+    if (r->m > 0) {
+        if (r->n <= 0 || r->n % P_BN != 0) return fail(NQ_ERROR_UNSUPPORTED, "all-reduce: job n must be a multiple of 256");
+        if (!r->flags) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: job flags");
+        const bool mc = r->mc_partial != nullptr;
+        if (mc) {
+            if (!r->mc_out || !r->mc_done || !aligned16(r->mc_partial) || !aligned16(r->mc_out))
+                return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: multicast addresses");
+        } else {
+            for (int p = 0; p < r->tp; ++p)
+                if (!r->peer_partial[p] || !r->peer_out[p] || !r->peer_done[p] || !aligned16(r->peer_partial[p]) ||
+                    !aligned16(r->peer_out[p]))
+                    return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: peer pointers");
+        }
+        ar->m = r->m;
+        ar->n = r->n;
+        ar->flags = r->flags;
+        ar->mc_partial = static_cast<uint8_t*>(r->mc_partial);
+        ar->mc_out = static_cast<uint8_t*>(r->mc_out);
+        ar->mc_done = r->mc_done;
+        for (int p = 0; p < r->tp; ++p) {
+            ar->peer_partial[p] = static_cast<const uint8_t*>(r->peer_partial[p]);
+            ar->peer_out[p] = static_cast<uint8_t*>(r->peer_out[p]);
+            ar->peer_done[p] = r->peer_done[p];
+        }
+    }
+    if (r->done_target) {
+        if (!r->done) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: done counter");
+        ar->done = r->done;
+        ar->done_target = r->done_target;
+    }
+    return NQ_SUCCESS;
+}
+}  // namespace
+
 nq_status_t gemm_allreduce_impl(const nq_gemm_desc_t* d, const nq_allreduce_desc_t* r, const void* a, const void* b,
-                                cudaStream_t s) {
-    if (!d || !r) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: null descriptor");
+                                void* out, cudaStream_t s) {
+    if (!d) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: null descriptor");
     if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: sizes must be positive");
-    if (!a || !b) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: null operand");
+    if (!a || !b || !out) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: null operand");
     const bool i8 = d->a_format == NQ_INT8;
     if (i8 != (d->b_format == NQ_INT8)) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: INT8 needs both operands INT8");
     if (d->a_format < NQ_E4M3 || d->a_format > NQ_INT8 || d->b_format < NQ_E4M3 || d->b_format > NQ_INT8)
         return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: format");
     if (d->b_layout != NQ_B_KN && d->b_layout != NQ_B_NK) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: b_layout");
-    if (d->out_dtype != NQ_BF16 || d->epilogue != NQ_EPI_NONE)
-        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: bf16 output without a fused activation only");
-    if (d->n % P_BN != 0 || d->k % 16 != 0 || !aligned16(a) || !aligned16(b))
-        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: needs n % 256 == 0, k % 16 == 0, 16-byte aligned operands");
-    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp || r->epoch == 0)
-        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: tp / rank / epoch");
-    if (!r->partial || !r->out || !r->flags || !r->done || !aligned16(r->partial) || !aligned16(r->out))
-        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: partial / out / flags / done");
-    const bool mc = r->mc_partial != nullptr;
-    if (mc && (!r->mc_out || !r->mc_done || !aligned16(r->mc_partial) || !aligned16(r->mc_out)))
-        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: multicast addresses");
-    for (int p = 0; p < r->tp; ++p) {
-        if (!r->peer_flags[p]) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: peer_flags");
-        if (!mc && (!r->peer_partial[p] || !r->peer_out[p] || !r->peer_done[p] || !aligned16(r->peer_partial[p]) ||
-                    !aligned16(r->peer_out[p])))
-            return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: peer pointers");
-    }
-    DeviceInfo di;
-    nq_status_t st = current_device(&di);
-    if (st != NQ_SUCCESS) return st;
+    if (d->epilogue != NQ_EPI_NONE && d->epilogue != NQ_EPI_SWIGLU)
+        return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_allreduce: epilogue");
+    const bool swiglu = d->epilogue == NQ_EPI_SWIGLU;
+    if (d->out_dtype != NQ_BF16) return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: bf16 output only");
+    if (d->k % 16 != 0 || d->n % 16 != 0 || !aligned16(a) || !aligned16(b) || !aligned16(out))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: needs k, n % 16 == 0 and 16-byte aligned operands");
+    if (swiglu && (i8 || d->n % P_BN != 0))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: SwiGLU needs FP8 operands and n % 256 == 0");
     ArParams ar;
-    std::memset(&ar, 0, sizeof(ar));
-    ar.tp = r->tp;
-    ar.rank = r->rank;
-    ar.epoch = r->epoch;
-    ar.mc_partial = static_cast<uint8_t*>(r->mc_partial);
-    ar.mc_out = static_cast<uint8_t*>(r->mc_out);
-    ar.mc_done = r->mc_done;
-    ar.flags = r->flags;
-    ar.done = r->done;
-    for (int p = 0; p < r->tp; ++p) {
-        ar.peer_flags[p] = r->peer_flags[p];
-        ar.peer_partial[p] = static_cast<const uint8_t*>(r->peer_partial[p]);
-        ar.peer_out[p] = static_cast<uint8_t*>(r->peer_out[p]);
-        ar.peer_done[p] = r->peer_done[p];
-    }
-    Epi ep{r->partial, d->n, NQ_BF16, d->alpha, d->row_scale, d->col_scale, d->bias};
+    nq_status_t st = fill_ar(r, &ar);
+    if (st != NQ_SUCCESS) return st;
+    if (ar.signal && (swiglu || d->n % P_BN != 0))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_allreduce: a signalling GEMM needs n % 256 == 0 and no fused activation");
+    DeviceInfo di;
+    st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    Epi ep{out, swiglu ? d->n / 2 : d->n, NQ_BF16, d->alpha, d->row_scale, d->col_scale, d->bias};
     const bool kn = d->b_layout == NQ_B_KN;
-    if (i8) return kn ? launch_tc2<true, true, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar)
-                      : launch_tc2<true, false, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar);
-    return kn ? launch_tc2<false, true, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar)
-              : launch_tc2<false, false, 1, false, true>(*d, a, b, r->partial, ep, s, di, &ar);
+    if (swiglu)
+        return kn ? launch_tc2<false, true, 1, true, true>(*d, a, b, out, ep, s, di, &ar)
+                  : launch_tc2<false, false, 1, true, true>(*d, a, b, out, ep, s, di, &ar);
+    if (i8) return kn ? launch_tc2<true, true, 1, false, true>(*d, a, b, out, ep, s, di, &ar)
+                      : launch_tc2<true, false, 1, false, true>(*d, a, b, out, ep, s, di, &ar);
+    return kn ? launch_tc2<false, true, 1, false, true>(*d, a, b, out, ep, s, di, &ar)
+              : launch_tc2<false, false, 1, false, true>(*d, a, b, out, ep, s, di, &ar);
+}
+
+nq_status_t allreduce_finish_impl(const nq_allreduce_desc_t* r, cudaStream_t s) {
+    ArParams ar;
+    nq_status_t st = fill_ar(r, &ar);
+    if (st != NQ_SUCCESS) return st;
+    if (ar.signal) return fail(NQ_ERROR_INVALID_VALUE, "nq_allreduce_finish: nothing to signal without a GEMM");
+    if (ar.m == 0 && ar.done_target == 0) return NQ_SUCCESS;
+    DeviceInfo di;
+    st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    // owned tiles spread over one group per SM
+    const int owned = ar.m > 0 ? (nq_gemm_allreduce_counters(ar.m, ar.n) + ar.tp - 1) / ar.tp : 1;
+    const int grid = std::max(1, std::min(owned, di.sm_count));
+    k_ar_finish<<<grid, AR_WARPS * 32, 0, s>>>(ar, device_error_word());
+    NQ_LAUNCH_CHECK("nq_allreduce_finish");
+    return NQ_SUCCESS;
 }
 
 }  // namespace nq
@@ -1518,9 +1576,15 @@ int nq_gemm_allreduce_counters(int m, int n) {
     return ((m + nq::P_BM - 1) / nq::P_BM) * ((n + nq::P_BN - 1) / nq::P_BN);
 }
 
+int nq_allreduce_done_per_job(int m, int n) { return nq_gemm_allreduce_counters(m, n) * nq::AR_WARPS; }
+
 nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* d, const nq_allreduce_desc_t* a_r, const void* a, const void* b,
-                              nq_stream_t s) {
-    return nq::gemm_allreduce_impl(d, a_r, a, b, s);
+                              void* out, nq_stream_t s) {
+    return nq::gemm_allreduce_impl(d, a_r, a, b, out, s);
+}
+
+nq_status_t nq_allreduce_finish(const nq_allreduce_desc_t* a_r, nq_stream_t s) {
+    return nq::allreduce_finish_impl(a_r, s);
 }
 
 // Test hook: the same GEMM forced onto the SIMT kernel (exact sequential-k).

@@ -101,12 +101,21 @@ def _as_tensor(w):
 
 
 # ---- fused GEMM + all-reduce over peer memory -------------------------------------
+class _ArState:
+    """Symmetric buffers and counters of one m x n all-reduced output split
+    into token chunks, and the epoch (forward count) of its counters."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
 class SymmetricAllReduce:
     """Symmetric buffers (torch.distributed._symmetric_memory: the same
     allocation mapped into every rank of `group`, plus an NVSwitch multicast
-    mapping when the box has one) for nq_gemm_allreduce: per output shape a
-    bf16 partial and a bf16 output buffer, and the per-tile arrival counters
-    and the completion counter, zeroed once.  mode "nvls" reduces through
+    mapping when the box has one) for the fused all-reduce of libnova_q
+    (nq_gemm_allreduce / nq_allreduce_finish): per output shape and chunking
+    a bf16 partial and a bf16 output buffer, the per-tile arrival counters of
+    every chunk and one completion counter.  mode "nvls" reduces through
     multimem (needs multicast), "p2p" through peer loads and stores, "auto"
     picks nvls when multicast is present."""
 
@@ -120,63 +129,89 @@ class SymmetricAllReduce:
         self.rank, self.tp = dist.get_rank(self.group), dist.get_world_size(self.group)
         if self.tp > capi.MAX_TP:
             raise ValueError(f"the fused all-reduce supports up to {capi.MAX_TP} ranks")
+        if mode not in ("auto", "nvls", "p2p"):
+            raise ValueError("mode must be 'auto', 'nvls' or 'p2p'")
         self.mode = mode
-        self._shapes = {}
+        self._states = {}
 
     def _map(self, t):
-        """(local, [peer pointers], multicast pointer or 0) of a symmetric tensor."""
+        """([peer pointers], multicast pointer or 0, handle) of a symmetric tensor."""
         h = self.symm.rendezvous(t, self.group.group_name)
         base = h.buffer_ptrs[self.rank]
         off = t.data_ptr() - base
         if off < 0 or off + t.numel() * t.element_size() > h.buffer_size:
             raise RuntimeError("symmetric tensor outside its allocation")
         mc = h.multicast_ptr + off if h.multicast_ptr else 0
-        return h, [p + off for p in h.buffer_ptrs], mc
+        return [p + off for p in h.buffer_ptrs], mc, h
 
-    def buffers(self, m, n):
-        """(partial, out, nq_allreduce_desc_t) for an m x n bf16 output, the
-        descriptor's epoch advanced for this call.  Each shape has its own
-        buffers and counters (zeroed on every rank before any rank can signal:
-        a barrier follows the clear); they live as long as the layer, since
-        peers may still be reading one when this rank moves to another shape."""
-        key = (m, n)
-        if key not in self._shapes:
+    def state(self, m, n, bounds):
+        """Buffers for an m x n bf16 output reduced in the token chunks
+        `bounds`, created (collectively: every rank calls in the same order)
+        on first use.  Counters are zeroed on every rank before any rank can
+        signal (a barrier follows the clear).  States live as long as the
+        layer: peers may still be reading a buffer when this rank moves to
+        another shape."""
+        key = (m, n, tuple(bounds))
+        if key not in self._states:
             t, nq = self.torch, self.nq
             dev = t.device("cuda", t.cuda.current_device())
-            tiles = nq.gemm_allreduce_counters(m, n)
-            flags = self.symm.empty(tiles, dtype=t.int32, device=dev)
+            offs, tiles = [], 0
+            for r0, r1 in bounds:
+                offs.append(tiles)
+                tiles += nq.gemm_allreduce_counters(r1 - r0, n)
+            flags = self.symm.empty(max(tiles, 1), dtype=t.int32, device=dev)
             done = self.symm.empty(16, dtype=t.int32, device=dev)
             partial = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
             out = self.symm.empty(m, n, dtype=t.bfloat16, device=dev)
             flags.zero_()
             done.zero_()
             t.cuda.synchronize()
-            hf, pf, _ = self._map(flags)
-            hd, pd, mcd = self._map(done)
-            hp, pp, mcp = self._map(partial)
-            ho, po, mco = self._map(out)
+            pf, _, hf = self._map(flags)
+            pd, mcd, hd = self._map(done)
+            pp, mcp, hp = self._map(partial)
+            po, mco, ho = self._map(out)
             self.dist.barrier(group=self.group)
             have_mc = bool(mcp and mco and mcd)
             use_mc = self.mode == "nvls" or (self.mode == "auto" and have_mc)
             if use_mc and not have_mc:
                 raise RuntimeError("NVSwitch multicast is not available for these buffers (mode 'nvls')")
-            d = nq.AllreduceDesc()
-            d.tp, d.rank, d.epoch = self.tp, self.rank, 0
-            d.partial, d.out = partial.data_ptr(), out.data_ptr()
-            if use_mc:
-                d.mc_partial, d.mc_out, d.mc_done = mcp, mco, mcd
-            d.flags, d.done = flags.data_ptr(), done.data_ptr()
-            for r in range(self.tp):
-                d.peer_flags[r], d.peer_done[r] = pf[r], pd[r]
-                d.peer_partial[r], d.peer_out[r] = pp[r], po[r]
-            self._shapes[key] = (partial, out, d, (flags, done, hf, hd, hp, ho))
-        partial, out, d, _ = self._shapes[key]
-        d.epoch += 1
-        return partial, out, d
+            per_forward = sum(nq.allreduce_done_per_job(r1 - r0, n) for r0, r1 in bounds)
+            self._states[key] = _ArState(m=m, n=n, bounds=list(bounds), offs=offs, flags=flags, done=done,
+                                         partial=partial, out=out, pf=pf, pd=pd, pp=pp, po=po, mcp=mcp, mco=mco,
+                                         mcd=mcd, use_mc=use_mc, per_forward=per_forward, epoch=0,
+                                         handles=(hf, hd, hp, ho))
+        return self._states[key]
 
-    @property
+    def begin(self, st):
+        """Advances the state's epoch: call once per forward, before its descriptors."""
+        st.epoch += 1
+
+    def desc(self, st, signal=None, job=None, finish=False):
+        """nq_allreduce_desc_t: `signal` = chunk whose partial the GEMM writes,
+        `job` = chunk to reduce, `finish` = wait for every chunk of this epoch."""
+        nq = self.nq
+        d = nq.AllreduceDesc()
+        d.tp, d.rank, d.epoch = self.tp, self.rank, st.epoch
+        if signal is not None:
+            d.signal = 1
+            for r in range(self.tp):
+                d.signal_flags[r] = st.pf[r] + 4 * st.offs[signal]
+        if job is not None:
+            r0, r1 = st.bounds[job]
+            row = 2 * r0 * st.n
+            d.m, d.n = r1 - r0, st.n
+            d.flags = st.flags.data_ptr() + 4 * st.offs[job]
+            if st.use_mc:
+                d.mc_partial, d.mc_out, d.mc_done = st.mcp + row, st.mco + row, st.mcd
+            for r in range(self.tp):
+                d.peer_partial[r], d.peer_out[r], d.peer_done[r] = st.pp[r] + row, st.po[r] + row, st.pd[r]
+        if finish:
+            d.done = st.done.data_ptr()
+            d.done_target = st.epoch * st.per_forward
+        return d
+
     def multicast(self):
-        return any(v[2].mc_partial for v in self._shapes.values())
+        return any(v.use_mc for v in self._states.values())
 
 
 # ---- layers ------------------------------------------------------------------------
@@ -301,15 +336,19 @@ class RowParallelLayer:
             return output
         xq, sx = self.lin.act(input, T)
         if self.fused is not None:
-            _, out, ard = self.fused.buffers(T, self.out_features)
+            # one kernel: the GEMM, its tiles' all-reduce and the completion wait
+            ar = self.fused
+            st = ar.state(T, self.out_features, [(0, T)])
+            ar.begin(st)
             lin, nq = self.lin, self.lin.nq
             d = nq.make_desc(T, lin.n, lin.k, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, sx.data_ptr(),
                              lin.s.data_ptr(), 0)
-            nq.gemm_allreduce(d, ard, xq.data_ptr(), lin.q.data_ptr(), self.torch.cuda.current_stream().cuda_stream)
+            nq.gemm_allreduce(d, ar.desc(st, signal=0, job=0, finish=True), xq.data_ptr(), lin.q.data_ptr(),
+                              st.partial.data_ptr(), self.torch.cuda.current_stream().cuda_stream)
             if output is None:
-                output = out
+                output = st.out
             else:
-                output.copy_(out)
+                output.copy_(st.out)
             if sync:
                 self.torch.cuda.current_stream().synchronize()
             return output
@@ -387,9 +426,7 @@ class TensorParallelMLP:
         down = self.down.lin
         xq, sx = self.gate_up.act(input, T)
         if self.down.fused is not None:
-            # one gate/up GEMM, then the down GEMM with the all-reduce fused in
-            self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)
-            return self.down.forward(h, output, batch, seq, sync)
+            return self._forward_fused(xq, sx, h, output, T, sync)
         bounds = chunk_bounds(T, self.chunks)
         if self.overlap == "down" or len(bounds) == 1:
             self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)
@@ -402,6 +439,41 @@ class TensorParallelMLP:
             return output[r0:r1]
 
         reduce_pipeline(bounds, compute, self.group, self.tp)
+        if sync:
+            t.cuda.current_stream().synchronize()
+        return output
+
+    def _forward_fused(self, xq, sx, h, output, T, sync):
+        """Token chunks c = 0..C-1: gate/up GEMM of chunk c (its reducer warps
+        all-reduce chunk c-1), quantize h, down GEMM of chunk c writing this
+        rank's partial and signalling its tiles; the last down GEMM also
+        reduces its own chunk and waits until every chunk is complete."""
+        t, nq = self.torch, self.gate_up.nq
+        s = t.cuda.current_stream().cuda_stream
+        ar, down, gu = self.down.fused, self.down.lin, self.gate_up
+        bounds = chunk_bounds(T, self.chunks)
+        st = ar.state(T, self.H, bounds)
+        ar.begin(st)
+        C = len(bounds)
+        for c, (r0, r1) in enumerate(bounds):
+            d1 = nq.make_desc(r1 - r0, gu.n, gu.k, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, sx.data_ptr() + 4 * r0,
+                              gu.s.data_ptr(), 0, nq.EPI_SWIGLU)
+            if c == 0:
+                nq.gemm(d1, xq.data_ptr() + r0 * gu.k, gu.q.data_ptr(), h.data_ptr() + 2 * r0 * self.I_local, s)
+            else:
+                nq.gemm_allreduce(d1, ar.desc(st, job=c - 1), xq.data_ptr() + r0 * gu.k, gu.q.data_ptr(),
+                                  h.data_ptr() + 2 * r0 * self.I_local, s)
+            hq, sh = down.act(h, T, r0, r1)
+            d2 = nq.make_desc(r1 - r0, down.n, down.k, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0,
+                              sh.data_ptr() + 4 * r0, down.s.data_ptr(), 0)
+            last = c == C - 1
+            nq.gemm_allreduce(d2, ar.desc(st, signal=c, job=c if last else None, finish=last),
+                              hq.data_ptr() + r0 * down.k, down.q.data_ptr(),
+                              st.partial.data_ptr() + 2 * r0 * self.H, s)
+        if output is None:
+            output = st.out
+        else:
+            output.copy_(st.out)
         if sync:
             t.cuda.current_stream().synchronize()
         return output

@@ -50,27 +50,38 @@ def test_status_strings_and_errors_without_gpu():
 
 
 def test_gemm_allreduce_argument_checks_without_gpu():
-    """nq_gemm_allreduce validates its descriptors before touching a device."""
+    """nq_gemm_allreduce / nq_allreduce_finish validate their descriptors
+    before touching a device."""
     import ctypes as C
     import nova_b200.capi as capi
     assert capi.lib.nq_gemm_allreduce_counters(16384, 8192) == 64 * 32
     assert capi.lib.nq_gemm_allreduce_counters(300, 512) == 2 * 2
     assert capi.lib.nq_gemm_allreduce_counters(0, 512) == 0
+    assert capi.lib.nq_allreduce_done_per_job(300, 512) == 4 * 5
     d = capi.make_desc(256, 512, 256)
     ar = capi.AllreduceDesc()
-    ar.tp, ar.rank = 2, 0
-    assert capi.gemm_allreduce.raw(None, C.byref(ar), 16, 16, None) == 1          # null descriptor
-    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 1    # no buffers
-    ar.partial, ar.out, ar.flags, ar.done = 256, 512, 1024, 2048
-    ar.tp = 9
-    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 1    # tp > NQ_MAX_TP
-    ar.tp = 2
+    ar.tp, ar.rank, ar.epoch = 2, 0, 1
+    run = lambda: capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, 16, None)
+    assert capi.gemm_allreduce.raw(None, C.byref(ar), 16, 16, 16, None) == 1     # null descriptor
+    ar.epoch = 0
+    assert run() == 1                                                              # epoch 0
+    ar.epoch, ar.tp = 1, 9
+    assert run() == 1                                                              # tp > NQ_MAX_TP
+    ar.tp, ar.signal = 2, 1
+    assert run() == 1                                                              # signal without counters
+    ar.signal_flags[0], ar.signal_flags[1] = 64, 128
     d.n = 384
-    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 2    # n % 256 != 0: unsupported
+    assert run() == 2                                                              # signalling needs n % 256 == 0
     d.n, d.out_dtype = 512, capi.F32
-    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 2    # bf16 output only
+    assert run() == 2                                                              # bf16 output only
     d.out_dtype = capi.BF16
-    assert capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, None) == 1    # peer pointers missing
+    ar.m, ar.n = 256, 512
+    assert run() == 1                                                              # job without counters
+    ar.flags = 256
+    assert run() == 1                                                              # job without peer pointers
+    assert capi.allreduce_finish.raw(C.byref(ar), None) == 1                       # finish cannot signal
+    ar.signal, ar.m, ar.done_target = 0, 0, 5
+    assert capi.allreduce_finish.raw(C.byref(ar), None) == 1                       # finish without a counter
 
 
 def test_no_device_is_an_error_not_a_crash():

@@ -47,7 +47,7 @@ def main():
             dist.all_reduce(errs, op=dist.ReduceOp.MAX)
             if rank == 0:
                 h_err, out_err, full_err = check_mlp(bits(out), [bits(h) for h in hs], x, wg, wu, wd, world)
-                mc = mlp.down.fused.multicast if mlp.down.fused is not None else False
+                mc = mlp.down.fused.multicast() if mlp.down.fused is not None else False
                 print(f"allreduce={allreduce} multicast={mc} T={T} H={H} I={I} tp={world} overlap={overlap} "
                       f"h_err={h_err:.3e} out_err={out_err:.3e} full_norm_err={full_err:.3e} "
                       f"replicated={bool(flag.item())} device_errors={int(errs.item())}", flush=True)
