@@ -378,7 +378,7 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20)):
     return out
 
 
-def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4, overlap="full", allreduce="auto"):
+def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=None, overlap="full", allreduce="auto"):
     """the FP8 SwiGLU MLP (nova_b200.tp.TensorParallelMLP)
     with tp = world size, T tokens per step (strong scaling: the same T at
     every tp).  x ~ N(0,1) bf16, weights ~ N(0,0.02) fp32 generated on the
@@ -423,7 +423,7 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=4,
     res = {"workload": "tp_fp8_swiglu_mlp (BASELINE configs[4])", "tokens": T, "hidden": H, "intermediate": I,
            "tp": world, "allreduce": (("fused-nvls" if mlp.down.fused.multicast() else "fused-p2p") if fused
                                       else ("nccl" if world > 1 else "none")),
-           "chunks": chunks if not fused else 1, "overlap": overlap, "ms_per_step": round(ms, 4),
+           "chunks": mlp.chunks, "overlap": overlap if not fused else "fused", "ms_per_step": round(ms, 4),
            "tokens_per_s": T / (ms * 1e-3), "tflops_total": tflops,
            "frac_of_tp_x_fp8_peak": tflops / (world * fp8_peak),
            "allreduce_bytes": 2 * T * H if world > 1 else 0, "scaling": "strong"}
@@ -470,7 +470,7 @@ def main():
     ap.add_argument("--cublas", action="store_true", help="also time cuBLASLt FP8 on the same shape")
     ap.add_argument("--no-secondary", action="store_true", help="skip the quantize bandwidth sweep")
     ap.add_argument("--no-tp-mlp", action="store_true", help="skip the TP SwiGLU MLP (configs[4]) block")
-    ap.add_argument("--tp-chunks", type=int, default=4)
+    ap.add_argument("--tp-chunks", type=int, default=None, help="token chunks of the TP pipeline (default: by tp)")
     ap.add_argument("--tp-overlap", choices=["full", "down"], default="full")
     ap.add_argument("--tp-allreduce", choices=["auto", "nvls", "p2p", "nccl"], default="auto")
     args = ap.parse_args()
