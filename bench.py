@@ -321,7 +321,8 @@ def run_ours(args):
         line["library_comparison"] = cublaslt_fp8(args.steps, args.warmup,
                                                   torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda"))
     if not args.no_secondary:
-        line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"])}
+        sizes = tuple(int(v) for v in args.sweep_sizes.split(","))
+        line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps), **c3_c4_bench(pk)}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
@@ -331,7 +332,7 @@ def run_ours(args):
     return 0
 
 
-def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20)):
+def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20), reps=None):
     """HBM-bound kernels of the path at the sweep sizes (fp32 input ~N(0,1)).
     Algorithmic bytes: quantize 5 B/elem (4 read + 1 write), amax 4 B/elem,
     calibrate+quantize 5 B/elem compulsory (9 B/elem as two passes), dequant
@@ -362,20 +363,105 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20)):
         for name, bpe, fn in cases:
             for _ in range(3):
                 fn()
-            reps = 20 if n <= (1 << 20) else 5
+            nrep = reps if reps else (20 if n <= (1 << 20) else 5)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             e0.record()
-            for _ in range(reps):
+            for _ in range(nrep):
                 fn()
             e1.record()
             torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / reps
+            ms = e0.elapsed_time(e1) / nrep
             gbs = bpe * n / (ms * 1e-3) / 1e9
             out.append({"kernel": name, "n": n, "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
                         "frac_hbm": round(gbs / hbm_gbs, 3)})
         del x, q, y, xb
     return out
+
+
+def _time_flushed(fn, reps, flush):
+    """Mean CUDA-event time (ms) of fn() with an L2 flush before each launch."""
+    import torch
+    for _ in range(3):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return sum(ts) / len(ts)
+
+
+def c3_c4_bench(pk, reps=20):
+    """BASELINE configs[2] and [3] on one GPU.
+    C3, W8A8 FP8 MLP up-projection: X 8192 x 4096 bf16 ~N(0,1) with 41 of
+    4096 channels x20; W 4096 x 14336 ~N(0,0.02), per-output-channel E4M3
+    (nq_quantize_cols); per-token E4M3 quantize of X (nq_quantize_rows) then
+    the GEMM with row/col scales in the epilogue, bf16 out: 9.621e11 flop.
+    C4, decode INT8 W8A8: W 28672 x 8192 (N x K) int8 per-channel, X M x 8192
+    int8 per-token, int32 accumulation, bf16 out; bytes = K*N + M*K + 2*M*N +
+    4*(M+N).  L2 flushed (256 MiB write) before every timed launch."""
+    import torch
+    import nova_b200.capi as nq
+    s = torch.cuda.current_stream().cuda_stream
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    res = {}
+    g = torch.Generator(device="cuda").manual_seed(4)
+    Mx, Kx, Nx = 8192, 4096, 14336
+    x = torch.randn(Mx, Kx, device="cuda", generator=g)
+    out_ch = torch.randperm(Kx, generator=torch.Generator().manual_seed(5))[:41].cuda()
+    x[:, out_ch] *= 20.0
+    x = x.to(torch.bfloat16)
+    w = torch.randn(Kx, Nx, device="cuda", generator=g).mul_(0.02)
+    wq = torch.empty(Kx, Nx, dtype=torch.uint8, device="cuda")
+    ws = torch.empty(Nx, device="cuda")
+    nq.quantize_cols(w.data_ptr(), wq.data_ptr(), ws.data_ptr(), Kx, Nx, nq.E4M3, s)
+    del w
+    xq = torch.empty(Mx, Kx, dtype=torch.uint8, device="cuda")
+    xs = torch.empty(Mx, device="cuda")
+    y = torch.empty(Mx, Nx, dtype=torch.bfloat16, device="cuda")
+    d = nq.make_desc(Mx, Nx, Kx, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, xs.data_ptr(), ws.data_ptr(), 0)
+    quant = lambda: nq.quantize_rows(x.data_ptr(), nq.BF16, xq.data_ptr(), xs.data_ptr(), Mx, Kx, nq.E4M3, s)
+    gemm = lambda: nq.gemm(d, xq.data_ptr(), wq.data_ptr(), y.data_ptr(), s)
+    flop = 2.0 * Mx * Nx * Kx
+    t_q = _time_flushed(quant, reps, flush)
+    t_g = _time_flushed(gemm, reps, flush)
+    t_all = _time_flushed(lambda: (quant(), gemm()), reps, flush)
+    res["c3_w8a8_up_proj"] = {
+        "m": Mx, "k": Kx, "n": Nx, "per_token_quant_us": round(t_q * 1e3, 1),
+        "per_token_quant_GBps": round((3 * Mx * Kx + 4 * Mx) / (t_q * 1e-3) / 1e9, 1),
+        "gemm_us": round(t_g * 1e3, 1), "gemm_tflops": round(flop / (t_g * 1e-3) / 1e12, 1),
+        "layer_us": round(t_all * 1e3, 1), "layer_tflops": round(flop / (t_all * 1e-3) / 1e12, 1),
+        "layer_frac_fp8_peak": round(flop / (t_all * 1e-3) / 1e12 / fp8_peak, 3),
+        "note": "layer = per-token quantize launch + GEMM launch (two kernels; the quantize is not fused into the GEMM prologue)"}
+    del x, xq, y, wq
+    torch.cuda.empty_cache()
+    Kd, Nd = 8192, 28672
+    wi = torch.randint(-127, 128, (Nd, Kd), dtype=torch.int8, device="cuda", generator=g)
+    sw = torch.rand(Nd, device="cuda", generator=g).mul_(1e-3)
+    c4 = []
+    for Md in (16, 64, 256):
+        xi = torch.randint(-127, 128, (Md, Kd), dtype=torch.int8, device="cuda", generator=g)
+        sx = torch.rand(Md, device="cuda", generator=g).mul_(1e-2)
+        yo = torch.empty(Md, Nd, dtype=torch.bfloat16, device="cuda")
+        dd = nq.make_desc(Md, Nd, Kd, nq.INT8, nq.INT8, nq.B_NK, nq.BF16, 1.0, sx.data_ptr(), sw.data_ptr(), 0)
+        t = _time_flushed(lambda: nq.gemm(dd, xi.data_ptr(), wi.data_ptr(), yo.data_ptr(), s), reps, flush)
+        byts = Kd * Nd + Md * Kd + 2 * Md * Nd + 4 * (Md + Nd)
+        gbs = byts / (t * 1e-3) / 1e9
+        c4.append({"m": Md, "us": round(t * 1e3, 1), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 3),
+                   "tops": round(2.0 * Md * Nd * Kd / (t * 1e-3) / 1e12, 1)})
+    res["c4_decode_int8"] = c4
+    del wi, flush
+    torch.cuda.empty_cache()
+    assert nq.device_error_flags() == 0
+    return res
 
 
 def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=None, overlap="full", allreduce="auto"):
@@ -473,11 +559,29 @@ def main():
     ap.add_argument("--tp-chunks", type=int, default=None, help="token chunks of the TP pipeline (default: by tp)")
     ap.add_argument("--tp-overlap", choices=["full", "down"], default="full")
     ap.add_argument("--tp-allreduce", choices=["auto", "nvls", "p2p", "nccl"], default="auto")
+    ap.add_argument("--only", choices=["all", "gemm", "sweep", "c3c4"], default="all",
+                    help="gemm: the headline GEMM line alone; sweep / c3c4: one secondary workload alone")
+    ap.add_argument("--sweep-sizes", default="1048576,58720256,234881024")
+    ap.add_argument("--sweep-reps", type=int, default=0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.only in ("sweep", "c3c4"):
+        # one secondary workload alone (a small, self-contained command for ncu captures)
+        import torch
+        torch.cuda.set_device(0)
+        pk = peaks()
+        if args.only == "sweep":
+            sizes = tuple(int(v) for v in args.sweep_sizes.split(","))
+            res = quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps)
+        else:
+            res = c3_c4_bench(pk)
+        print(json.dumps({"only": args.only, "result": res}), flush=True)
+        return 0
+    if args.only == "gemm":
+        args.no_secondary = args.no_tp_mlp = args.no_cpu_baseline = True
     return run_ours(args)
 
 
