@@ -138,6 +138,17 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def spin_up(fn, seconds):
+    """Runs fn back to back for about `seconds` so that the SM clock has left
+    its idle state before the warm-up steps (an idle B200 sits at ~120 MHz)."""
+    import torch
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+
+
 def make_operands(seed_a=2, seed_b=3):
     """A, B ~ N(0,1) quantized on the GPU with per-tensor amax/448 scales
     (nq_calibrate_quantize: amax -> scale -> OCP E4M3 codes)."""
@@ -230,6 +241,7 @@ def run_ours(args):
     def gemm():
         nq.gemm(desc, qa.data_ptr(), qb.data_ptr(), out.data_ptr(), sh)
 
+    spin_up(gemm, 0.1)
     for _ in range(args.warmup):
         flush.zero_()
         gemm()
@@ -361,9 +373,9 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20), reps=None):
             ("per-token quantize bf16 -> e4m3 (4096 cols)", 3.0, lambda: nq.quantize_rows(xb.data_ptr(), nq.BF16, q.data_ptr(), rs.data_ptr(), rows, cols, nq.E4M3, s)),
         ]
         for name, bpe, fn in cases:
-            for _ in range(3):
+            for _ in range(10):
                 fn()
-            nrep = reps if reps else (20 if n <= (1 << 20) else 5)
+            nrep = reps if reps else (20 if n <= (64 << 20) else 10)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             e0.record()
@@ -382,7 +394,7 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20), reps=None):
 def _time_flushed(fn, reps, flush):
     """Mean CUDA-event time (ms) of fn() with an L2 flush before each launch."""
     import torch
-    for _ in range(3):
+    for _ in range(10):
         flush.zero_()
         fn()
     torch.cuda.synchronize()
@@ -489,7 +501,7 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=No
     x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
     fused = mlp.down.fused is not None
     out = None if fused else torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
-    for _ in range(warmup):
+    for _ in range(max(warmup, 5)):
         mlp.forward(x, out, 1, T, sync=False)
     torch.cuda.synchronize()
     barrier(world)
