@@ -139,8 +139,10 @@ def max_over_ranks(v, world):
 
 
 def spin_up(fn, seconds):
-    """Runs fn back to back for about `seconds` so that the SM clock has left
-    its idle state before the warm-up steps (an idle B200 sits at ~120 MHz)."""
+    """Runs fn back to back for about `seconds` so that the clocks have left
+    their idle state before anything is timed (an idle B200 sits at ~120 MHz
+    SM clock, and a few launches after idle time memory-bound kernels at
+    60-75% of the bandwidth they reach once the GPU is busy)."""
     import torch
     t_end = time.perf_counter() + seconds
     while time.perf_counter() < t_end:
@@ -241,7 +243,7 @@ def run_ours(args):
     def gemm():
         nq.gemm(desc, qa.data_ptr(), qb.data_ptr(), out.data_ptr(), sh)
 
-    spin_up(gemm, 0.1)
+    spin_up(lambda: (flush.zero_(), gemm()), 0.3)
     for _ in range(args.warmup):
         flush.zero_()
         gemm()
@@ -373,8 +375,7 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20), reps=None):
             ("per-token quantize bf16 -> e4m3 (4096 cols)", 3.0, lambda: nq.quantize_rows(xb.data_ptr(), nq.BF16, q.data_ptr(), rs.data_ptr(), rows, cols, nq.E4M3, s)),
         ]
         for name, bpe, fn in cases:
-            for _ in range(10):
-                fn()
+            spin_up(fn, 0.02)
             nrep = reps if reps else (20 if n <= (64 << 20) else 10)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
@@ -394,10 +395,7 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20), reps=None):
 def _time_flushed(fn, reps, flush):
     """Mean CUDA-event time (ms) of fn() with an L2 flush before each launch."""
     import torch
-    for _ in range(10):
-        flush.zero_()
-        fn()
-    torch.cuda.synchronize()
+    spin_up(lambda: (flush.zero_(), fn()), 0.02)
     ts = []
     for _ in range(reps):
         flush.zero_()
