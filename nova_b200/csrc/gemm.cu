@@ -665,6 +665,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         const bool raw_s32 = INT8_KIND && OUTK == 0 && ep.out_dtype == NQ_S32;
         int it = 0;
         int chunk_seq = 0;  // chunks stored by this warp so far (selects the staging slot)
+        // AR signal: the previous tile, counted on its owner once its stores are
+        // complete -- one tile later, so the epilogue never waits on its own stores
+        int sig_pending = -1;
         for (int u = cluster; u < num_units; u += nclusters, ++it) {
             const Unit un = decode_unit(u, st, kblocks);
             const int tile = un.tile;
@@ -774,6 +777,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 }
                 continue;
             }
+            int tile_groups = 0;  // bulk store groups this warp commits for this tile
             // this warp's 128 columns, 32 per tcgen05.ld, the next 32 in flight
             uint32_t r[32];
             uint4 w[8];
@@ -872,20 +876,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                     bulk_commit_group();
                 }
                 ++chunk_seq;
+                ++tile_groups;
             }
             if constexpr (AR) {
                 if (ar.signal) {
-                    // this warp's part of the partial tile is in memory: count it on the owner
-                    if (lane == 0) {
-                        bulk_wait_group_all();
+                    // the previous tile's part of this warp is in memory (every bulk group
+                    // but the chunks just issued for this tile has completed): count it
+                    if (lane == 0 && sig_pending >= 0) {
+                        switch (tile_groups) {
+                            case 0: bulk_wait_group<0>(); break;
+                            case 1: bulk_wait_group<1>(); break;
+                            case 2: bulk_wait_group<2>(); break;
+                            case 3: bulk_wait_group<3>(); break;
+                            default: bulk_wait_group<4>(); break;
+                        }
                         fence_proxy_async_global();
-                        red_add_release_sys(ar.signal_flags[tile % ar.tp] + tile, 1u);
+                        red_add_release_sys(ar.signal_flags[sig_pending % ar.tp] + sig_pending, 1u);
                     }
                     __syncwarp();
+                    sig_pending = tile;
                 }
             }
         }
         if (lane == 0) bulk_wait_group_all();
+        if constexpr (AR) {
+            if (ar.signal && lane == 0 && sig_pending >= 0) {
+                fence_proxy_async_global();
+                red_add_release_sys(ar.signal_flags[sig_pending % ar.tp] + sig_pending, 1u);
+            }
+        }
     }
     __syncwarp();  // reconverge the producer / MMA warps before the aligned cluster barrier
     tc_fence_before();
