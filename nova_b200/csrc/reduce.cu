@@ -281,41 +281,6 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows(const In* __restrict__ 
     else pass(std::false_type{});
 }
 
-// Per-row scaled quantize with the row held in registers: one read of the
-// row from HBM.  Each thread owns up to VPT 16-byte vectors (8 bf16 or 4 fp32
-// values each) of the row; cols * sizeof(In) must be a multiple of 16 and at
-// most VPT * 16 * blockDim.x bytes.
-template <int F, class In, int VPT>
-__global__ void __launch_bounds__(kThreads) k_quant_rows_reg(const In* __restrict__ src, uint8_t* __restrict__ dst,
-                                                             float* __restrict__ scales, int cols) {
-    constexpr int EPV = 16 / sizeof(In);  // elements per vector
-    const size_t r = blockIdx.x;
-    const uint4* row = reinterpret_cast<const uint4*>(src + r * static_cast<size_t>(cols));
-    uint8_t* out = dst + r * static_cast<size_t>(cols);
-    const int nv = cols / EPV;
-    uint4 v[VPT];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        const int idx = threadIdx.x + k * kThreads;
-        v[k] = idx < nv ? __ldg(row + idx) : make_uint4(0u, 0u, 0u, 0u);
-    }
-    float a = 0.0f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k)
-#pragma unroll
-        for (int e = 0; e < EPV; ++e) a = fmaxf(a, fabsf(vec_elem<In>(v[k], e)));
-    a = block_minmax(FLT_MAX, a).y;
-    const RowScale rs = row_scale<F>(a);
-    if (threadIdx.x == 0) scales[r] = rs.s;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        const int idx = threadIdx.x + k * kThreads;
-        if (idx >= nv) break;
-        if (rs.mul) encode_vec<F, In, true>(v[k], out + idx * EPV, rs);
-        else encode_vec<F, In, false>(v[k], out + idx * EPV, rs);
-    }
-}
-
 // Per-row scaled quantize with rows staged whole in shared memory by 1-D bulk
 // copies: a persistent grid, block b owning rows b, b + gridDim.x, ...; a
 // ring of `stages` row buffers keeps the next rows streaming in from HBM
@@ -380,6 +345,78 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows_bulk(const In* __restri
     if (!ok && threadIdx.x == 0) {
         // a wait gave up: let the copies still in flight land before the block exits
         for (int j = i; j < i + stages && row_of(j) < rows; ++j)
+            dev::mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, nullptr);
+    }
+}
+
+// Per-row scaled quantize, one warp per row, for rows of up to 12 KB: each
+// warp streams its rows (global warp w takes rows w, w + warps, ...) through a
+// private ring of `stages` row buffers filled by 1-D bulk copies, and reduces
+// the row amax with shuffles -- no block barrier per row, so short rows from
+// many warps are in flight at once.  Row bytes must be a multiple of 16 and
+// src 16-byte aligned.
+template <int F, class In>
+__global__ void __launch_bounds__(kThreads) k_quant_rows_warp(const In* __restrict__ src, uint8_t* __restrict__ dst,
+                                                              float* __restrict__ scales, int rows, int cols,
+                                                              int stages, uint32_t* err) {
+    extern __shared__ __align__(128) uint8_t q_smem[];
+    constexpr int EPV = 16 / sizeof(In);
+    constexpr int kWarps = kThreads / 32;
+    const uint32_t rb = static_cast<uint32_t>(cols) * sizeof(In);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    uint8_t* ring = q_smem + static_cast<size_t>(warp) * stages * rb;
+    uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + static_cast<size_t>(kWarps) * stages * rb) + warp * stages;
+    const int nv = cols / EPV;
+    if (lane == 0) {
+        for (int k = 0; k < stages; ++k) dev::mbar_init(&full[k], 1);
+        dev::fence_mbar_init();
+    }
+    __syncwarp();
+    const long long gw = static_cast<long long>(blockIdx.x) * kWarps + warp;
+    const long long nw = static_cast<long long>(gridDim.x) * kWarps;
+    const char* base = reinterpret_cast<const char*>(src);
+    auto issue = [&](int i) {
+        const long long r = gw + i * nw;
+        if (r >= rows) return;
+        const int st = i % stages;
+        dev::mbar_arrive_expect_tx(&full[st], rb);
+        dev::bulk_load_1d(ring + static_cast<size_t>(st) * rb, base + r * rb, rb, &full[st]);
+    };
+    if (lane == 0)
+        for (int i = 0; i < stages; ++i) issue(i);
+    int i = 0;
+    bool ok = true;
+    for (;; ++i) {
+        const long long r = gw + i * nw;
+        if (r >= rows) break;
+        const int st = i % stages;
+        ok = dev::mbar_wait(&full[st], static_cast<uint32_t>(i / stages) & 1u, err);
+        if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+        }
+        const uint4* buf = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(st) * rb);
+        float a = 0.0f;
+        for (int v = lane; v < nv; v += 32) {
+            const uint4 q = buf[v];
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) a = fmaxf(a, fabsf(vec_elem<In>(q, e)));
+        }
+        a = warp_max(a);
+        const RowScale rs = row_scale<F>(a);
+        if (lane == 0) scales[r] = rs.s;
+        uint8_t* out = dst + r * cols;
+        if (rs.mul) {
+            for (int v = lane; v < nv; v += 32) encode_vec<F, In, true>(buf[v], out + v * EPV, rs);
+        } else {
+            for (int v = lane; v < nv; v += 32) encode_vec<F, In, false>(buf[v], out + v * EPV, rs);
+        }
+        __syncwarp();  // every lane is done with buffer st
+        if (lane == 0) issue(i + stages);
+    }
+    if (!ok && lane == 0) {
+        for (int j = i; j < i + stages && gw + j * nw < rows; ++j)
             dev::mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, nullptr);
     }
 }
@@ -463,6 +500,44 @@ nq_status_t launch_quant_rows_bulk(const void* src, nq_dtype_t dt, uint8_t* dst,
     };
     if (dt == NQ_F32) return launch(k_quant_rows_bulk<F, float>, static_cast<const float*>(src));
     return launch(k_quant_rows_bulk<F, uint16_t>, static_cast<const uint16_t*>(src));
+}
+
+constexpr size_t kWarpRowMax = 12 * 1024;  // rows up to this size take k_quant_rows_warp
+
+// Ring depth per warp: about 24 KB of rows (2 .. 8 stages); grid: every block
+// that fits on the device at once, at most one warp per row.
+template <int F>
+nq_status_t launch_quant_rows_warp(const void* src, nq_dtype_t dt, uint8_t* dst, float* scales, int rows, int cols,
+                                   const DeviceInfo& di, cudaStream_t s) {
+    const size_t rb = static_cast<size_t>(cols) * (dt == NQ_F32 ? 4 : 2);
+    const int stages = static_cast<int>(std::max<size_t>(2, std::min<size_t>(8, (24 * 1024) / rb)));
+    constexpr int warps = kThreads / 32;
+    const int smem = static_cast<int>(warps * stages * rb + warps * stages * 8);
+    auto launch = [&](auto kern, const auto* typed_src) -> nq_status_t {
+        static std::mutex mu;
+        static uint64_t attr_set = 0;
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            const uint64_t bit = 1ull << (di.device & 63);
+            if (!(attr_set & bit)) {
+                NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                              "cudaFuncSetAttribute(quantize_rows)");
+                attr_set |= bit;
+            }
+        }
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        const long long want = (static_cast<long long>(rows) + warps - 1) / warps;
+        const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, static_cast<long long>(di.sm_count) * per_sm)));
+        kern<<<grid, kThreads, smem, s>>>(typed_src, dst, scales, rows, cols, stages, device_error_word());
+        NQ_LAUNCH_CHECK("nq_quantize_rows (warp)");
+        return NQ_SUCCESS;
+    };
+    if (dt == NQ_F32) return launch(k_quant_rows_warp<F, float>, static_cast<const float*>(src));
+    return launch(k_quant_rows_warp<F, uint16_t>, static_cast<const uint16_t*>(src));
 }
 
 namespace {
@@ -667,42 +742,25 @@ nq_status_t nq_quantize_rows(const void* src, nq_dtype_t src_dtype, uint8_t* dst
     if (st != NQ_SUCCESS) return st;
     using namespace nq::dev;
     const size_t row_bytes = static_cast<size_t>(cols) * (src_dtype == NQ_F32 ? 4 : 2);
-    // rows of 4 KB .. 100 KB: bulk-staged ring, persistent grid
-    if (row_bytes % 16 == 0 && nq::aligned16(src) && row_bytes >= 4096 && 2 * row_bytes <= nq::kBulkRowSmem &&
-        reinterpret_cast<uintptr_t>(dst) % (src_dtype == NQ_F32 ? 4 : 8) == 0) {
+    const bool staged = row_bytes % 16 == 0 && nq::aligned16(src) &&
+                        reinterpret_cast<uintptr_t>(dst) % (src_dtype == NQ_F32 ? 4 : 8) == 0;
+    // rows up to 12 KB: one warp per row, bulk-staged per-warp ring
+    if (staged && row_bytes <= nq::kWarpRowMax) {
+        switch (fmt) {
+            case NQ_E4M3: return nq::launch_quant_rows_warp<kE4M3>(src, src_dtype, dst, scales, rows, cols, di, s);
+            case NQ_E5M2: return nq::launch_quant_rows_warp<kE5M2>(src, src_dtype, dst, scales, rows, cols, di, s);
+            case NQ_INT8: return nq::launch_quant_rows_warp<kINT8>(src, src_dtype, dst, scales, rows, cols, di, s);
+            default: return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: format");
+        }
+    }
+    // rows of 12 KB .. 100 KB: one block per row, bulk-staged ring, persistent grid
+    if (staged && 2 * row_bytes <= nq::kBulkRowSmem) {
         switch (fmt) {
             case NQ_E4M3: return nq::launch_quant_rows_bulk<kE4M3>(src, src_dtype, dst, scales, rows, cols, di, s);
             case NQ_E5M2: return nq::launch_quant_rows_bulk<kE5M2>(src, src_dtype, dst, scales, rows, cols, di, s);
             case NQ_INT8: return nq::launch_quant_rows_bulk<kINT8>(src, src_dtype, dst, scales, rows, cols, di, s);
             default: return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: format");
         }
-    }
-    // narrower rows, register-resident: one HBM read per element
-    const bool reg_ok = row_bytes % 16 == 0 && nq::aligned16(src) && row_bytes <= 4u * 16u * nq::kThreads &&
-                        reinterpret_cast<uintptr_t>(dst) % (src_dtype == NQ_F32 ? 4 : 8) == 0;
-    if (reg_ok) {
-        const int vpt_need = static_cast<int>((row_bytes / 16 + nq::kThreads - 1) / nq::kThreads);
-#define NQ_QROWS_REG(F, VPT)                                                                                       \
-    (src_dtype == NQ_F32 ? nq::k_quant_rows_reg<F, float, VPT><<<rows, nq::kThreads, 0, s>>>(                      \
-                               static_cast<const float*>(src), dst, scales, cols)                                  \
-                         : nq::k_quant_rows_reg<F, uint16_t, VPT><<<rows, nq::kThreads, 0, s>>>(                   \
-                               static_cast<const uint16_t*>(src), dst, scales, cols))
-#define NQ_QROWS_REG_F(F)                            \
-    do {                                             \
-        if (vpt_need <= 1) NQ_QROWS_REG(F, 1);       \
-        else if (vpt_need <= 2) NQ_QROWS_REG(F, 2);  \
-        else NQ_QROWS_REG(F, 4);                     \
-    } while (0)
-        switch (fmt) {
-            case NQ_E4M3: NQ_QROWS_REG_F(kE4M3); break;
-            case NQ_E5M2: NQ_QROWS_REG_F(kE5M2); break;
-            case NQ_INT8: NQ_QROWS_REG_F(kINT8); break;
-            default: return fail(NQ_ERROR_INVALID_VALUE, "nq_quantize_rows: format");
-        }
-#undef NQ_QROWS_REG_F
-#undef NQ_QROWS_REG
-        NQ_LAUNCH_CHECK("nq_quantize_rows");
-        return NQ_SUCCESS;
     }
 #define NQ_QROWS(F)                                                                                       \
     (src_dtype == NQ_F32                                                                                  \
