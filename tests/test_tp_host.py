@@ -118,3 +118,51 @@ def _gloo_rank(rank, world, port, case):
 def test_reduce_pipeline_two_gloo_ranks(case):
     import torch.multiprocessing as mp
     mp.start_processes(_gloo_rank, args=(2, _free_port(), case), nprocs=2, join=True, start_method="spawn")
+
+
+def test_fused_allreduce_descriptors():
+    """The descriptors the chunked MLP pipeline hands to nq_gemm_allreduce:
+    per-chunk counter offsets, job rows offset into the symmetric buffers,
+    the completion target of an epoch (host logic only, fake addresses)."""
+    import nova_b200.capi as nq
+    ar = object.__new__(tp.SymmetricAllReduce)
+    ar.nq, ar.tp, ar.rank = nq, 4, 1
+    T, n = 1300, 512
+    bounds = tp.chunk_bounds(T, 3)
+    assert len(bounds) == 3
+    offs, tiles = [], 0
+    for r0, r1 in bounds:
+        offs.append(tiles)
+        tiles += nq.gemm_allreduce_counters(r1 - r0, n)
+
+    class FakeT:
+        def __init__(self, p):
+            self.p = p
+
+        def data_ptr(self):
+            return self.p
+
+    per_forward = sum(nq.allreduce_done_per_job(r1 - r0, n) for r0, r1 in bounds)
+    st = tp._ArState(m=T, n=n, bounds=bounds, offs=offs, flags=FakeT(1 << 20), done=FakeT(2 << 20),
+                     partial=FakeT(3 << 20), out=FakeT(4 << 20), pf=[(10 + r) << 20 for r in range(4)],
+                     pd=[(20 + r) << 20 for r in range(4)], pp=[(30 + r) << 20 for r in range(4)],
+                     po=[(40 + r) << 20 for r in range(4)], mcp=50 << 20, mco=60 << 20, mcd=70 << 20,
+                     use_mc=True, per_forward=per_forward, epoch=0)
+    ar.begin(st)
+    ar.begin(st)
+    assert st.epoch == 2
+    d = ar.desc(st, signal=1)
+    assert d.signal == 1 and d.m == 0 and d.done_target == 0 and d.epoch == 2
+    assert [d.signal_flags[r] for r in range(4)] == [((10 + r) << 20) + 4 * offs[1] for r in range(4)]
+    r0, r1 = bounds[2]
+    d = ar.desc(st, signal=2, job=2, finish=True)
+    assert (d.m, d.n) == (r1 - r0, n)
+    assert d.flags == (1 << 20) + 4 * offs[2]
+    assert d.mc_partial == (50 << 20) + 2 * r0 * n and d.mc_out == (60 << 20) + 2 * r0 * n
+    assert d.mc_done == 70 << 20 and d.done == 2 << 20
+    assert d.done_target == 2 * per_forward
+    assert [d.peer_partial[r] for r in range(4)] == [((30 + r) << 20) + 2 * r0 * n for r in range(4)]
+    st.use_mc = False
+    d = ar.desc(st, job=0)
+    assert d.mc_partial is None and d.peer_out[3] == (43 << 20)
+    assert per_forward == 5 * tiles
