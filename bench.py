@@ -393,19 +393,19 @@ def quantize_sweep(hbm_gbs, sizes=(1 << 20, 56 << 20, 224 << 20), reps=None):
 
 
 def _time_flushed(fn, reps, flush):
-    """Mean CUDA-event time (ms) of fn() with an L2 flush before each launch."""
+    """Mean CUDA-event time (ms) of fn() with an L2 flush before each launch;
+    all launches are enqueued back to back (one synchronize at the end), so
+    the GPU never idles between them."""
     import torch
     spin_up(lambda: (flush.zero_(), fn()), 0.02)
-    ts = []
-    for _ in range(reps):
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for e0, e1 in evs:
         flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
         e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1))
-    return sum(ts) / len(ts)
+    torch.cuda.synchronize()
+    return sum(e0.elapsed_time(e1) for e0, e1 in evs) / reps
 
 
 def c3_c4_bench(pk, reps=20):
