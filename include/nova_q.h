@@ -220,9 +220,9 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  * (:406).  Here the all-reduce runs inside the GEMM kernels, over NVLink:
  *
  *  signal  the GEMM's output is a partial: its bf16 tiles go to the `out`
- *          argument (this rank's partial buffer) and every epilogue warp adds
- *          1 (16 per 256 x 256 tile) to the tile's counter on the tile's
- *          owner rank (tile % tp);
+ *          argument (this rank's partial buffer); once a 256 x 256 tile's
+ *          stores are complete a signaller warp adds 1 to the tile's counter
+ *          on the tile's owner rank (tile % tp);
  *  job     the kernel's reducer warps (5 per CTA pair, beside the GEMM's own
  *          warps) sum the tiles of an m x n output that this rank owns, once
  *          all tp ranks have signalled them, and write the bf16 sum to every
@@ -234,7 +234,7 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  *              peer pointers, fp32 sum in rank order, one bf16 rounding,
  *              stores to every peer;
  *          each reducer warp then counts itself on every rank's completion
- *          counter (5 counts per tile);
+ *          counter (nq_allreduce_done_per_job);
  *  finish  with done_target > 0 the kernel returns only once this rank's
  *          completion counter reaches done_target (its output buffer holds
  *          every reduced tile).
@@ -248,7 +248,7 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  * All buffers are symmetric allocations (same size on every rank, mapped into
  * every peer); job pointers address the job's first row.  Counters only
  * grow: zero before epoch 1; the n-th use of a counter set passes epoch n and
- * a job waits for its tiles' counters to reach epoch * tp * 16.  Every rank
+ * a job waits for its tiles' counters to reach epoch * tp.  Every rank
  * makes the same sequence of calls.  Waits on other GPUs give up after 5 s
  * and set the device error word (nq_device_error_flags).  A signalling GEMM
  * needs out_dtype NQ_BF16, epilogue NQ_EPI_NONE, n % 256 == 0; jobs need
@@ -276,8 +276,10 @@ typedef struct {
 
 /* Tiles (counters) of an m x n output. */
 int nq_gemm_allreduce_counters(int m, int n);
-/* Completion counts one job of an m x n output adds on every rank. */
-int nq_allreduce_done_per_job(int m, int n);
+/* Completion counts one job of an m x n output adds on every rank: 5 per tile,
+   4 when the kernel hosting the job also signals its own output (one of its
+   reducer warps is then the signaller). */
+int nq_allreduce_done_per_job(int m, int n, int in_signalling_kernel);
 nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* desc, const nq_allreduce_desc_t* ar,
                               const void* a, const void* b, void* out, nq_stream_t s);
 nq_status_t nq_allreduce_finish(const nq_allreduce_desc_t* ar, nq_stream_t s);

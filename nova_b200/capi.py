@@ -93,7 +93,7 @@ lib.nq_gemm_allreduce_counters.restype = C.c_int
 lib.nq_gemm_allreduce_counters.argtypes = [_i, _i]
 gemm_allreduce_counters = lib.nq_gemm_allreduce_counters
 lib.nq_allreduce_done_per_job.restype = C.c_int
-lib.nq_allreduce_done_per_job.argtypes = [_i, _i]
+lib.nq_allreduce_done_per_job.argtypes = [_i, _i, _i]
 allreduce_done_per_job = lib.nq_allreduce_done_per_job
 
 

@@ -424,8 +424,8 @@ constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_B
 // and 11 of both CTAs of a GEMM pair plus the second CTA's idle warp 1, or
 // one CTA of the finish kernel) takes the owned tiles i = group, group +
 // ngroups, ... of the job (owned tile i is tile rank + tp * i in the producing
-// GEMM's tile order); warp j of the group waits until all tp ranks' 16
-// epilogue warps have signalled the tile, then sums its rows j, j + AR_WARPS,
+// GEMM's tile order); warp j of the group waits until all tp ranks have
+// signalled the tile, then sums its rows j, j + nwarps,
 // ... over the ranks (multicast: multimem.ld_reduce, fp32 accumulation in the
 // switch; peer: fp32 sum in rank order) and writes the bf16 rows to every
 // rank's output, then counts itself on every rank's completion counter.
@@ -433,8 +433,8 @@ constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_B
 // rows in flight per warp.  Finally warp 0 of group 0 waits for done_target.
 constexpr int AR_WARPS = 5;
 constexpr int P_THREADS_AR = P_THREADS + 64;  // + warps 10, 11
-constexpr int AR_SIGNALS_PER_TILE = 2 * P_EPI_WARPS;
-__device__ __forceinline__ void ar_job(const ArParams& ar, int j, int group, int ngroups, uint32_t* err) {
+constexpr int AR_SIGNALS_PER_TILE = 1;  // the signaller's one count per tile and rank
+__device__ __forceinline__ void ar_job(const ArParams& ar, int j, int nwarps, int group, int ngroups, uint32_t* err) {
     const int lane = threadIdx.x & 31;
     bool ok = true;
     if (ar.m > 0) {
@@ -456,19 +456,19 @@ __device__ __forceinline__ void ar_job(const ArParams& ar, int j, int group, int
             const size_t base = static_cast<size_t>(r0) * pitch + static_cast<size_t>(nb) * P_BN * 2 + lane * 16;
             if (ar.mc_partial) {
                 constexpr int U = 10;
-                for (int r = j; r < rows; r += U * AR_WARPS) {
+                for (int r = j; r < rows; r += U * nwarps) {
                     uint4 v[U];
 #pragma unroll
                     for (int u = 0; u < U; ++u)
-                        if (r + u * AR_WARPS < rows)
-                            v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u * AR_WARPS) * pitch);
+                        if (r + u * nwarps < rows)
+                            v[u] = multimem_ld_reduce_bf16x8(ar.mc_partial + base + (r + u * nwarps) * pitch);
 #pragma unroll
                     for (int u = 0; u < U; ++u)
-                        if (r + u * AR_WARPS < rows) multimem_st_v4(ar.mc_out + base + (r + u * AR_WARPS) * pitch, v[u]);
+                        if (r + u * nwarps < rows) multimem_st_v4(ar.mc_out + base + (r + u * nwarps) * pitch, v[u]);
                 }
             } else {
                 constexpr int U = 4;
-                for (int r = j; r < rows; r += U * AR_WARPS) {
+                for (int r = j; r < rows; r += U * nwarps) {
                     float acc[U][8];
 #pragma unroll
                     for (int u = 0; u < U; ++u)
@@ -478,12 +478,12 @@ __device__ __forceinline__ void ar_job(const ArParams& ar, int j, int group, int
                         uint4 q[U];
 #pragma unroll
                         for (int u = 0; u < U; ++u)
-                            if (r + u * AR_WARPS < rows)
+                            if (r + u * nwarps < rows)
                                 q[u] = __ldcg(reinterpret_cast<const uint4*>(ar.peer_partial[p] + base +
-                                                                             (r + u * AR_WARPS) * pitch));
+                                                                             (r + u * nwarps) * pitch));
 #pragma unroll
                         for (int u = 0; u < U; ++u) {
-                            if (r + u * AR_WARPS >= rows) continue;
+                            if (r + u * nwarps >= rows) continue;
                             const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
@@ -494,11 +494,11 @@ __device__ __forceinline__ void ar_job(const ArParams& ar, int j, int group, int
                     }
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
-                        if (r + u * AR_WARPS >= rows) continue;
+                        if (r + u * nwarps >= rows) continue;
                         const uint4 o = make_uint4(f32x2_to_bf16x2(acc[u][0], acc[u][1]), f32x2_to_bf16x2(acc[u][2], acc[u][3]),
                                                    f32x2_to_bf16x2(acc[u][4], acc[u][5]), f32x2_to_bf16x2(acc[u][6], acc[u][7]));
                         for (int p = 0; p < ar.tp; ++p)
-                            __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u * AR_WARPS) * pitch), o);
+                            __stcg(reinterpret_cast<uint4*>(ar.peer_out[p] + base + (r + u * nwarps) * pitch), o);
                     }
                 }
             }
@@ -518,7 +518,34 @@ __device__ __forceinline__ void ar_job(const ArParams& ar, int j, int group, int
 
 // Job and / or finish without a GEMM: one CTA of AR_WARPS warps per group.
 __global__ void __launch_bounds__(AR_WARPS * 32) k_ar_finish(const __grid_constant__ ArParams ar, uint32_t* err) {
-    ar_job(ar, threadIdx.x >> 5, blockIdx.x, gridDim.x, err);
+    ar_job(ar, threadIdx.x >> 5, AR_WARPS, blockIdx.x, gridDim.x, err);
+}
+
+// Signaller of a GEMM whose output is a partial (ar.signal): one lane of the
+// first CTA's warp 11 walks this cluster's tiles in order, waits (bounded)
+// until both CTAs' 8 epilogue warps have counted the tile's stores complete on
+// the cluster counter, and adds 1 to the tile's counter on its owner rank.  The
+// system-scope release stays off the epilogue warps, which only do a
+// cluster-scope add.
+__device__ __forceinline__ void ar_signal_tiles(const ArParams& ar, uint32_t cnt_addr, int cluster, int nclusters,
+                                                int num_tiles, uint32_t* err) {
+    if ((threadIdx.x & 31) != 0) return;
+    uint32_t want = 0;
+    for (int t = cluster; t < num_tiles; t += nclusters) {
+        want += 2 * P_EPI_WARPS;
+        const uint64_t t0 = globaltimer();
+        bool ok = true;
+        while (ld_acquire_cluster(cnt_addr) < want) {
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                atomicOr(err, kErrWaitTimeout);
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (!ok) return;
+        red_add_release_sys(ar.signal_flags[t % ar.tp] + t, 1u);
+    }
 }
 
 // OUTK: 0 = 4-byte output (f32, or raw s32 for INT8) through TMA stores,
@@ -545,6 +572,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     uint64_t* tempty = tfull + 2;           // [2] leader: 16 epilogue warps -> MMA
     uint64_t* done = tempty + 2;            // leader: MMA drain
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint32_t* sig_cnt = tmem_slot + 1;      // AR: epilogue warps' completed tiles (first CTA)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -567,6 +595,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             mbar_init(&tempty[a], 2 * P_EPI_WARPS);
         }
         mbar_init(done, 1);
+        *sig_cnt = 0u;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -613,7 +642,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         // ---------------- MMA issuer (leader CTA only) ----------------
         if constexpr (AR) {
             // the second CTA's warp 1 is one of the reducers
-            if (rank == 1) ar_job(ar, 2, cluster, nclusters, err);
+            if (rank == 1) ar_job(ar, ar.signal ? 1 : 2, ar.signal ? AR_WARPS - 1 : AR_WARPS, cluster, nclusters, err);
         }
         if (rank == 0 && elect_one()) {
             int stage = 0;
@@ -653,8 +682,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         }
     } else if (AR && warp >= 2 + P_EPI_WARPS) {
         // ---------------- all-reduce (warps 10, 11 of both CTAs) ----------------
-        const int j = warp - 2 - P_EPI_WARPS + (rank == 0 ? 0 : 3);
-        ar_job(ar, j, cluster, nclusters, err);
+        // with ar.signal the first CTA's warp 11 is the signaller and 4 warps reduce
+        if (ar.signal && rank == 0 && warp == 3 + P_EPI_WARPS) {
+            ar_signal_tiles(ar, mapa_shared(smem_u32(sig_cnt), 0), cluster, nclusters, num_tiles, err);
+        } else {
+            const int j = warp - 2 - P_EPI_WARPS + (rank == 0 ? 0 : (ar.signal ? 2 : 3));
+            ar_job(ar, j, ar.signal ? AR_WARPS - 1 : AR_WARPS, cluster, nclusters, err);
+        }
     } else {
         // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
         const int quarter = warp & 3;            // TMEM lanes [32 * quarter, +32)
@@ -668,6 +702,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         // AR signal: the previous tile, counted on its owner once its stores are
         // complete -- one tile later, so the epilogue never waits on its own stores
         int sig_pending = -1;
+        const uint32_t sig_cnt_leader = mapa_shared(smem_u32(sig_cnt), 0);
         for (int u = cluster; u < num_units; u += nclusters, ++it) {
             const Unit un = decode_unit(u, st, kblocks);
             const int tile = un.tile;
@@ -891,7 +926,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                             default: bulk_wait_group<4>(); break;
                         }
                         fence_proxy_async_global();
-                        red_add_release_sys(ar.signal_flags[sig_pending % ar.tp] + sig_pending, 1u);
+                        red_add_release_cluster(sig_cnt_leader, 1u);
                     }
                     __syncwarp();
                     sig_pending = tile;
@@ -902,7 +937,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         if constexpr (AR) {
             if (ar.signal && lane == 0 && sig_pending >= 0) {
                 fence_proxy_async_global();
-                red_add_release_sys(ar.signal_flags[sig_pending % ar.tp] + sig_pending, 1u);
+                red_add_release_cluster(sig_cnt_leader, 1u);
             }
         }
     }
@@ -1595,7 +1630,9 @@ int nq_gemm_allreduce_counters(int m, int n) {
     return ((m + nq::P_BM - 1) / nq::P_BM) * ((n + nq::P_BN - 1) / nq::P_BN);
 }
 
-int nq_allreduce_done_per_job(int m, int n) { return nq_gemm_allreduce_counters(m, n) * nq::AR_WARPS; }
+int nq_allreduce_done_per_job(int m, int n, int in_signalling_kernel) {
+    return nq_gemm_allreduce_counters(m, n) * (in_signalling_kernel ? nq::AR_WARPS - 1 : nq::AR_WARPS);
+}
 
 nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* d, const nq_allreduce_desc_t* a_r, const void* a, const void* b,
                               void* out, nq_stream_t s) {

@@ -81,6 +81,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     }
 }
 
+// Cluster-scope release add / acquire load on a shared::cluster address (mapa).
+__device__ __forceinline__ void red_add_release_cluster(uint32_t cluster_saddr, uint32_t v) {
+    asm volatile("red.release.cluster.shared::cluster.add.u32 [%0], %1;" ::"r"(cluster_saddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_cluster(uint32_t cluster_saddr) {
+    uint32_t v;
+    asm volatile("ld.acquire.cluster.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_saddr) : "memory");
+    return v;
+}
+
 // ---- NVLink peer memory and NVSwitch multicast (multimem) ------------------------
 // System-scope release add (a peer GPU's counter through its UVA address).
 __device__ __forceinline__ void red_add_release_sys(uint32_t* p, uint32_t v) {

@@ -175,7 +175,10 @@ class SymmetricAllReduce:
             use_mc = self.mode == "nvls" or (self.mode == "auto" and have_mc)
             if use_mc and not have_mc:
                 raise RuntimeError("NVSwitch multicast is not available for these buffers (mode 'nvls')")
-            per_forward = sum(nq.allreduce_done_per_job(r1 - r0, n) for r0, r1 in bounds)
+            # chunk c < C-1 is reduced by a gate/up GEMM (5 reducer warps), the
+            # last chunk by its own signalling down GEMM (4 reducer warps)
+            per_forward = sum(nq.allreduce_done_per_job(r1 - r0, n, int(c == len(bounds) - 1))
+                              for c, (r0, r1) in enumerate(bounds))
             self._states[key] = _ArState(m=m, n=n, bounds=list(bounds), offs=offs, flags=flags, done=done,
                                          partial=partial, out=out, pf=pf, pd=pd, pp=pp, po=po, mcp=mcp, mco=mco,
                                          mcd=mcd, use_mc=use_mc, per_forward=per_forward, epoch=0,

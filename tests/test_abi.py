@@ -57,7 +57,8 @@ def test_gemm_allreduce_argument_checks_without_gpu():
     assert capi.lib.nq_gemm_allreduce_counters(16384, 8192) == 64 * 32
     assert capi.lib.nq_gemm_allreduce_counters(300, 512) == 2 * 2
     assert capi.lib.nq_gemm_allreduce_counters(0, 512) == 0
-    assert capi.lib.nq_allreduce_done_per_job(300, 512) == 4 * 5
+    assert capi.lib.nq_allreduce_done_per_job(300, 512, 0) == 4 * 5
+    assert capi.lib.nq_allreduce_done_per_job(300, 512, 1) == 4 * 4
     d = capi.make_desc(256, 512, 256)
     ar = capi.AllreduceDesc()
     ar.tp, ar.rank, ar.epoch = 2, 0, 1

@@ -142,7 +142,8 @@ def test_fused_allreduce_descriptors():
         def data_ptr(self):
             return self.p
 
-    per_forward = sum(nq.allreduce_done_per_job(r1 - r0, n) for r0, r1 in bounds)
+    per_forward = sum(nq.allreduce_done_per_job(r1 - r0, n, int(c == len(bounds) - 1))
+                      for c, (r0, r1) in enumerate(bounds))
     st = tp._ArState(m=T, n=n, bounds=bounds, offs=offs, flags=FakeT(1 << 20), done=FakeT(2 << 20),
                      partial=FakeT(3 << 20), out=FakeT(4 << 20), pf=[(10 + r) << 20 for r in range(4)],
                      pd=[(20 + r) << 20 for r in range(4)], pp=[(30 + r) << 20 for r in range(4)],
@@ -165,4 +166,5 @@ def test_fused_allreduce_descriptors():
     st.use_mc = False
     d = ar.desc(st, job=0)
     assert d.mc_partial is None and d.peer_out[3] == (43 << 20)
-    assert per_forward == 5 * tiles
+    last = nq.gemm_allreduce_counters(bounds[-1][1] - bounds[-1][0], n)
+    assert per_forward == 5 * (tiles - last) + 4 * last
