@@ -23,13 +23,16 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     ok = True
     modes = sys.argv[1:] or ["nccl", "p2p", "auto"]
-    cases = [(600, 256, 512, "full"), (1024, 512, 1024, "down"), (1000, 512, 2048, "full"), (600, 256, 512, "full")]
+    # (T, H, I, overlap, chunks): chunks None = the layer's default for this tp;
+    # 3 exercises the chunked pipeline (jobs hosted by the gate/up GEMMs) at any tp
+    cases = [(600, 256, 512, "full", None), (1024, 512, 1024, "down", None), (1000, 512, 2048, "full", 3),
+             (600, 256, 512, "full", None)]
     for allreduce in modes:
-        for T, H, I, overlap in cases:
+        for T, H, I, overlap, chunks in cases:
             unit = 128 * world
             I = max(unit, (I + unit - 1) // unit * unit)   # each rank's shard a multiple of 128
             x, wg, wu, wd = weights(T, H, I)
-            mlp = TensorParallelMLP(H, I, overlap=overlap, allreduce=allreduce)
+            mlp = TensorParallelMLP(H, I, overlap=overlap, allreduce=allreduce, chunks=chunks)
             mlp.set_weight(wg, wu, wd)
             out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
             for _ in range(2):   # repeated calls: the fused path's counters must come back to zero
@@ -49,6 +52,7 @@ def main():
                 h_err, out_err, full_err = check_mlp(bits(out), [bits(h) for h in hs], x, wg, wu, wd, world)
                 mc = mlp.down.fused.multicast() if mlp.down.fused is not None else False
                 print(f"allreduce={allreduce} multicast={mc} T={T} H={H} I={I} tp={world} overlap={overlap} "
+                      f"chunks={mlp.chunks} "
                       f"h_err={h_err:.3e} out_err={out_err:.3e} full_norm_err={full_err:.3e} "
                       f"replicated={bool(flag.item())} device_errors={int(errs.item())}", flush=True)
                 ok = ok and h_err <= 1e-2 and out_err <= 1e-2 and full_err <= 1e-2 and bool(flag.item()) \
