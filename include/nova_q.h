@@ -99,6 +99,11 @@ nq_status_t nq_dequantize_int8_to_f32(const int8_t* src, float* dst, size_t n, f
 /* int8_kernels.hpp:75-79 (int8_kernels.cu:171-194) */
 nq_status_t nq_quantize_f32_to_int8_with_calibration(const float* src, int8_t* dst, size_t n,
                                                      float min_val, float max_val, nq_stream_t s);
+/* FakeQuantize::forward of quantization-aware training (qat.hpp:64-72) over a
+   device array: scale floored at 1e-6, q = clamp(round_half_away((x - zp) /
+   scale), +-127), dst = q * scale + zp (multiply, then add). */
+nq_status_t nq_fake_quantize_int8(const float* src, float* dst, size_t n, float scale,
+                                  float zero_point, nq_stream_t s);
 /* QuantizedTensor<int8_t>::FromFloat rounding (quantize_tensor.hpp:176-182):
    q = clamp(round_half_away(x/scale), +-127). */
 nq_status_t nq_quantize_f32_to_int8_round_away(const float* src, int8_t* dst, size_t n,

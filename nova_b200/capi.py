@@ -61,6 +61,7 @@ _SIGS = {
     "nq_dequantize_int8_to_f32": [_p, _p, _sz, _f, _f, _i, _p],
     "nq_quantize_f32_to_int8_with_calibration": [_p, _p, _sz, _f, _f, _p],
     "nq_quantize_f32_to_int8_round_away": [_p, _p, _sz, _f, _p],
+    "nq_fake_quantize_int8": [_p, _p, _sz, _f, _f, _p],
     "nq_compute_minmax": [_p, _sz, _p, _p, _p],
     "nq_build_histogram": [_p, _p, _sz, _f, _f, _i, _p],
     "nq_minmax_async": [_p, _sz, _p, _p],

@@ -263,6 +263,27 @@ __global__ void __launch_bounds__(256) k_dequant_batched(const uint8_t* const* s
     for (size_t i = nvec * 16 + t0; i < n; i += stride) d[i] = dev::compat_e4m3_decode(__ldg(s + i)) * mul;
 }
 
+// FakeQuantize::forward of QAT (qat.hpp:64-72) over an array: scale floored at
+// 1e-6, q = clamp(round_half_away((x - zp) / scale), +-127), y = q * scale + zp,
+// each step rounded once (no FMA), as the reference's host expression.
+__device__ __forceinline__ float fake_quant1(float x, float s, float zp) {
+    const float r = roundf(__fdiv_rn(__fsub_rn(x, zp), s));
+    const float c = fmaxf(-127.0f, fminf(127.0f, r));
+    return __fadd_rn(__fmul_rn(c, s), zp);
+}
+__global__ void __launch_bounds__(256) k_fake_quant(const float* __restrict__ src, float* __restrict__ dst, size_t n,
+                                                    int vec, float s, float zp) {
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t n4 = vec ? n / 4 : 0;
+    for (size_t v = t0; v < n4; v += stride) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(src) + v);
+        reinterpret_cast<float4*>(dst)[v] =
+            make_float4(fake_quant1(x.x, s, zp), fake_quant1(x.y, s, zp), fake_quant1(x.z, s, zp), fake_quant1(x.w, s, zp));
+    }
+    for (size_t i = n4 * 4 + t0; i < n; i += stride) dst[i] = fake_quant1(__ldg(src + i), s, zp);
+}
+
 // ---- launch helpers ------------------------------------------------------------------
 nq_status_t grid_for(size_t n, int* grid) {
     DeviceInfo di;
@@ -406,6 +427,19 @@ nq_status_t nq_quantize_f32_to_int8_round_away(const float* src, int8_t* dst, si
                                                nq_stream_t s) {
     return nq::launch_quant(src, reinterpret_cast<uint8_t*>(dst), n, nq::Int8RoundAway{scale}, s,
                             "nq_quantize_f32_to_int8_round_away");
+}
+
+nq_status_t nq_fake_quantize_int8(const float* src, float* dst, size_t n, float scale, float zero_point,
+                                  nq_stream_t s) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst) return fail(NQ_ERROR_INVALID_VALUE, "nq_fake_quantize_int8: null pointer");
+    int grid;
+    nq_status_t st = nq::grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    const float sc = scale < 1e-6f ? 1e-6f : scale;  // FakeQuantize::forward's floor (qat.hpp:65-66)
+    nq::k_fake_quant<<<grid, 256, 0, s>>>(src, dst, n, nq::aligned16(src) && nq::aligned16(dst), sc, zero_point);
+    NQ_LAUNCH_CHECK("nq_fake_quantize_int8");
+    return NQ_SUCCESS;
 }
 
 nq_status_t nq_quantize_scaled(const void* src, nq_dtype_t src_dtype, uint8_t* dst, size_t n, nq_format_t fmt,

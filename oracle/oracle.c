@@ -609,3 +609,17 @@ void orc_swiglu_epilogue(const float* acc, void* out, int out_bf16, int m, int n
             else ((float*)out)[(size_t)i * no + j] = h;
         }
 }
+
+/* FakeQuantize::forward (qat.hpp:64-72): scale floored at 1e-6, q =
+   clamp(round_half_away((x - zp) / scale), +-127), y = q * scale + zp with a
+   separate multiply and add (compiled with -ffp-contract=off). */
+void orc_fake_quantize_int8(const float* src, float* dst, size_t n, float scale, float zero_point) {
+    const float s = scale < 1e-6f ? 1e-6f : scale;
+    for (size_t i = 0; i < n; ++i) {
+        float r = roundf((src[i] - zero_point) / s);
+        float c = r < 127.0f ? r : 127.0f;     /* NaN -> 127, as std::min(127, NaN) */
+        c = -127.0f < c ? c : -127.0f;
+        const float m = c * s;
+        dst[i] = m + zero_point;
+    }
+}

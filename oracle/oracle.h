@@ -117,6 +117,9 @@ float orc_silu_mul(float g, float u);
 void orc_swiglu_epilogue(const float* acc, void* out, int out_bf16, int m, int n, float alpha,
                          const float* row_scale, const float* col_scale, const float* bias);
 
+/* QAT FakeQuantize::forward over an array (qat.hpp:64-72) */
+void orc_fake_quantize_int8(const float* src, float* dst, size_t n, float scale, float zero_point);
+
 /* bounded multi-threaded run of orc_fp8_gemm_reference over rows
    [row0, row0+rows); returns the number of threads used */
 int orc_fp8_gemm_reference_rows_mt(const uint8_t* a, const uint8_t* b, float* c, int m,

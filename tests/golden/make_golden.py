@@ -7,9 +7,12 @@ oracle/_ref/libnova_ref_host.so):
                      (include/cuda/quantize/fp8_types.hpp:64-207)
   from_float.npz     QuantizedTensor<int8_t>::FromFloat (quantize_tensor.hpp:160-191)
   quantized_matmul.npz  QuantizedMatmul::forward (quantize_ops.hpp:54-81)
+  qat_fake_quant.npz FakeQuantize::forward (qat.hpp:64-72) at several scales and
+                     zero points, edge inputs included
 
 Run from the repository root after `make -C oracle ref`:
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py          # every fixture
+    python tests/golden/make_golden.py qat      # qat_fake_quant.npz only
 """
 import ctypes as C
 import os
@@ -61,5 +64,27 @@ def main():
     print("golden fixtures written to", HERE)
 
 
+def qat():
+    r = O.ref_host()
+    if r is None:
+        raise SystemExit("oracle/_ref/libnova_ref_host.so missing: run `make -C oracle ref` first")
+    rng = np.random.default_rng(20261202)
+    edge = O.special_floats()
+    out = {}
+    for i, (scale, zp) in enumerate([(0.05, 0.0), (0.5, 2.0), (1e-8, 0.0), (3.0, -1.25), (0.0, 0.5)]):
+        x = np.concatenate([edge, (rng.standard_normal(3000) * 8.0).astype(np.float32),
+                            (np.arange(-300, 301, dtype=np.float32) * 0.5 * np.float32(max(scale, 1e-6)) + zp)])
+        x = x.astype(np.float32)
+        y = np.empty_like(x)
+        r.ref_fake_quantize(x.ctypes.data, y.ctypes.data, x.size, scale, zp)
+        out[f"x{i}"], out[f"y{i}"], out[f"p{i}"] = x, y, np.array([scale, zp], np.float32)
+    np.savez_compressed(os.path.join(HERE, "qat_fake_quant.npz"), **out)
+    print("qat_fake_quant.npz written to", HERE)
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "qat":
+        qat()
+    else:
+        main()
+        qat()

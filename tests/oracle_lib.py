@@ -48,6 +48,7 @@ for name, res, args in [
     ("orc_fp8_gemm_reference_rows_mt", _i, [_p, _p, _p, _i, _i, _i, _f, _f, _f, _i, _i, _i]),
     ("orc_swiglu_epilogue", None, [_p, _p, _i, _i, _i, _f, _p, _p, _p]),
     ("orc_silu_mul", _f, [_f, _f]),
+    ("orc_fake_quantize_int8", None, [_p, _p, _sz, _f, _f]),
 ]:
     fn = getattr(lib, name)
     fn.restype = res
@@ -209,6 +210,10 @@ def ref_host():
     r.ref_from_float_int8.restype = _i
     r.ref_from_float_int8.argtypes = [_p, _sz, _f, _p, _p]
     r.ref_quantized_matmul.argtypes = [_p, _p, _p, _i, _i, _i, _f, _f]
+    r.ref_fake_quantize.argtypes = [_p, _p, _sz, _f, _f]
+    r.ref_amp_load.restype = _i
+    r.ref_amp_load.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(_i), C.POINTER(_f), C.POINTER(_f), C.POINTER(_i)]
+    r.ref_amp_save_two.argtypes = [C.c_char_p]
     return r
 
 
@@ -294,3 +299,10 @@ def tp_down_partial(h_bits, wd, rank, tp):
     hq, sh = quantize_rows(np.ascontiguousarray(h_bits), 0, bf16=True)
     dq, ds = quantize_cols(np.ascontiguousarray(wd[rank * il:(rank + 1) * il]), 0)
     return epilogue(gemm_fp8_acc(hq, dq, 0, 0, True), True, 1.0, sh, ds)
+
+
+def fake_quantize(x, scale, zero_point):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib.orc_fake_quantize_int8(ptr(x), ptr(y), x.size, scale, zero_point)
+    return y

@@ -182,3 +182,19 @@ def test_rows_cols_quantize_oracle_consistency():
     assert sz[0] == 1.0 and not z.any()
     qc, sc = O.quantize_cols(x, 2)
     np.testing.assert_array_equal(qc.T, O.quantize_rows(np.ascontiguousarray(x.T), 2)[0])
+
+
+def test_fake_quantize_oracle_matches_reference_golden():
+    """QAT FakeQuantize::forward (qat.hpp:64-72): the oracle restatement is
+    bit-identical to the reference's own host code (golden vectors, and live
+    against the reference build when it is present)."""
+    g = np.load(os.path.join(GOLD, "qat_fake_quant.npz"))
+    r = O.ref_host()
+    for i in range(5):
+        x, y, (scale, zp) = g[f"x{i}"], g[f"y{i}"], g[f"p{i}"]
+        got = O.fake_quantize(x, float(scale), float(zp))
+        np.testing.assert_array_equal(got.view(np.uint32), y.view(np.uint32))
+        if r is not None:
+            live = np.empty_like(x)
+            r.ref_fake_quantize(O.ptr(x), O.ptr(live), x.size, float(scale), float(zp))
+            np.testing.assert_array_equal(live.view(np.uint32), y.view(np.uint32))

@@ -196,3 +196,32 @@ def test_invalid_arguments(nq):
     with pytest.raises(NqError):
         nq.quantize_f32_to_int8(0, 0, 10, 1.0, 0.0, 1, 0)
     nq.quantize_f32_to_int8(0, 0, 0, 1.0, 0.0, 1, 0)  # n == 0 is a no-op
+
+
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("off", [0, 4])
+def test_fake_quantize_bit_exact(nq, n, off):
+    """QAT FakeQuantize::forward over a device array (nq_fake_quantize_int8):
+    bit-identical to the oracle (itself pinned to the reference's host code),
+    on the vector body, the tail and unaligned pointers."""
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    x = rand(n, 7 + n, 5.0)
+    x[: min(n, 3)] = [0.025, -0.075, np.nan][: min(n, 3)]
+    for scale, zp in [(0.05, 0.0), (0.5, 2.0), (0.0, 0.5)]:
+        d_x, d_y = dev(x, off), empty(4 * n, off)
+        nq.fake_quantize_int8(ptr(d_x), ptr(d_y), n, scale, zp, stream())
+        got = host(d_y, np.float32)
+        np.testing.assert_array_equal(got.view(np.uint32), O.fake_quantize(x, scale, zp).view(np.uint32))
+
+
+def test_fake_quantize_reference_golden(nq):
+    import os
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "qat_fake_quant.npz"))
+    for i in range(5):
+        x, y, (scale, zp) = g[f"x{i}"], g[f"y{i}"], g[f"p{i}"]
+        d_x, d_y = dev(x), empty(4 * x.size)
+        nq.fake_quantize_int8(ptr(d_x), ptr(d_y), x.size, float(scale), float(zp), stream())
+        np.testing.assert_array_equal(host(d_y, np.float32).view(np.uint32), y.view(np.uint32))
