@@ -168,3 +168,21 @@ def test_fused_allreduce_descriptors():
     assert d.mc_partial is None and d.peer_out[3] == (43 << 20)
     last = nq.gemm_allreduce_counters(bounds[-1][1] - bounds[-1][0], n)
     assert per_forward == 5 * (tiles - last) + 4 * last
+
+
+def test_layer_argument_checks_without_gpu():
+    """Shape and option errors are raised on the host before any device work
+    (the reference throws std::invalid_argument, tensor_parallel_layers.cpp)."""
+    with pytest.raises(ValueError):
+        tp.TensorParallelMLP(256, 200)            # intermediate not a multiple of 128
+    with pytest.raises(ValueError):
+        tp.TensorParallelMLP(250, 256)            # hidden not a multiple of 16
+    with pytest.raises(ValueError):
+        tp.TensorParallelMLP(256, 256, overlap="sideways")
+    with pytest.raises(ValueError):
+        tp.RowParallelLayer(256, 256, allreduce="carrier-pigeon")
+    mlp = tp.TensorParallelMLP(256, 512)
+    assert (mlp.tp, mlp.rank, mlp.chunks, mlp.I_local) == (1, 0, 1, 512)
+    assert mlp.down.fused is None                 # tp = 1: no all-reduce at all
+    with pytest.raises(RuntimeError):
+        mlp.forward(None, None, 1, 4)             # weights not set
