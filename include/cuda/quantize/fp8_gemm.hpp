@@ -58,6 +58,28 @@ public:
         forward(grad_output, a, grad_b, n, m, k, g, stream);
     }
 
+    // Additive: the true gradients of output = (a.b) * scale_a * scale_b for a
+    // gradient grad_output (M x N) quantized with scale_grad, E4M3 or E5M2
+    // (nq_fp8_gemm_backward): grad_a = grad_output . b^T, grad_b = a^T . grad_output.
+    static void backward_exact(const FP8E4M3* grad_output, float scale_grad, const FP8E4M3* a, const FP8E4M3* b,
+                               float* grad_a, float* grad_b, int m, int k, int n, Config config = Config{},
+                               cudaStream_t stream = 0) {
+        detail::nq_report(nq_fp8_gemm_backward(reinterpret_cast<const uint8_t*>(grad_output), NQ_E4M3,
+                                               reinterpret_cast<const uint8_t*>(a), reinterpret_cast<const uint8_t*>(b),
+                                               grad_a, grad_b, m, k, n, scale_grad, config.scale_a, config.scale_b,
+                                               stream),
+                          "FP8GEMM::backward_exact");
+    }
+    static void backward_exact(const FP8E5M2* grad_output, float scale_grad, const FP8E4M3* a, const FP8E4M3* b,
+                               float* grad_a, float* grad_b, int m, int k, int n, Config config = Config{},
+                               cudaStream_t stream = 0) {
+        detail::nq_report(nq_fp8_gemm_backward(reinterpret_cast<const uint8_t*>(grad_output), NQ_E5M2,
+                                               reinterpret_cast<const uint8_t*>(a), reinterpret_cast<const uint8_t*>(b),
+                                               grad_a, grad_b, m, k, n, scale_grad, config.scale_a, config.scale_b,
+                                               stream),
+                          "FP8GEMM::backward_exact");
+    }
+
     static size_t get_workspace_size(int m, int k, int n, const Config&) { return nq_fp8_gemm_workspace_size(m, k, n); }
 };
 

@@ -300,6 +300,16 @@ nq_status_t nq_fp8_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, 
 nq_status_t nq_fp8e5m2_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k,
                                     int n, float scale_a, float scale_b, float scale_out,
                                     nq_stream_t s);
+/* Gradients of C = (A.B)*scale_a*scale_b for FP8 operands, with the transposes
+   FP8GEMM::backward omits (fp8_gemm.cu:200-230 passes A and B untransposed):
+     grad_a (M x K) = scale_grad*scale_b * grad_out (M x N) . B^T
+     grad_b (K x N) = scale_a*scale_grad * A^T . grad_out
+   A M x K and B K x N E4M3, grad_out M x N in grad_format (E4M3, or E5M2 for
+   the usual gradient range), fp32 outputs; either output may be NULL to skip
+   it.  grad_b transposes A once into pool scratch. */
+nq_status_t nq_fp8_gemm_backward(const uint8_t* grad_out, nq_format_t grad_format, const uint8_t* a,
+                                 const uint8_t* b, float* grad_a, float* grad_b, int m, int k, int n,
+                                 float scale_grad, float scale_a, float scale_b, nq_stream_t s);
 /* QuantizedMatmul::mixed_precision, quantize_ops.hpp:83-102 (W8 A32):
    out[i,j] = sum_p a[i,p] * (b[p,j] * scale_b[p]) in order, one rounding per
    multiply and add (the reference host loop); all pointers device. */

@@ -81,6 +81,7 @@ _SIGS = {
     "nq_fp8e5m2_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_device_error_flags": [_u32p, _i],
     "nq_mixed_precision_matmul": [_p, _p, _p, _p, _i, _i, _i, _p],
+    "nq_fp8_gemm_backward": [_p, _i, _p, _p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
 }
 
 lib.nq_status_string.restype = C.c_char_p

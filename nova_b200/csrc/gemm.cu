@@ -1469,6 +1469,24 @@ __global__ void __launch_bounds__(256) k_mixed_precision(const float* __restrict
     out[static_cast<size_t>(row) * N + col] = s;
 }
 
+// Byte transpose (rows x cols -> cols x rows) through 32 x 32 shared tiles,
+// coalesced on both sides; used to give a GEMM a K-major copy of an operand.
+__global__ void __launch_bounds__(256) k_transpose_u8(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                      int rows, int cols) {
+    __shared__ uint8_t tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 8 rows of 32 per pass
+    for (int y = ty; y < 32; y += 8) {
+        const int r = r0 + y, c = c0 + tx;
+        if (r < rows && c < cols) tile[y][tx] = src[static_cast<size_t>(r) * cols + c];
+    }
+    __syncthreads();
+    for (int y = ty; y < 32; y += 8) {
+        const int c = c0 + y, r = r0 + tx;
+        if (c < cols && r < rows) dst[static_cast<size_t>(c) * rows + r] = tile[tx][y];
+    }
+}
+
 }  // namespace
 
 nq_status_t gemm_impl(const nq_gemm_desc_t* d, const void* a, const void* b, void* out, cudaStream_t s,
@@ -1669,6 +1687,54 @@ nq_status_t nq_fp8_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, 
 nq_status_t nq_fp8e5m2_gemm_forward(const uint8_t* a, const uint8_t* b, float* out, int m, int k, int n, float scale_a,
                                     float scale_b, float scale_out, nq_stream_t s) {
     return fp8_forward(a, b, out, m, k, n, scale_a, scale_b, scale_out, NQ_E5M2, s);
+}
+
+nq_status_t nq_fp8_gemm_backward(const uint8_t* grad_out, nq_format_t grad_format, const uint8_t* a, const uint8_t* b,
+                                 float* grad_a, float* grad_b, int m, int k, int n, float scale_grad, float scale_a,
+                                 float scale_b, nq_stream_t s) {
+    if (m < 0 || k < 0 || n < 0) return nq::fail(NQ_ERROR_INVALID_VALUE, "nq_fp8_gemm_backward: negative size");
+    if (grad_format != NQ_E4M3 && grad_format != NQ_E5M2)
+        return nq::fail(NQ_ERROR_INVALID_VALUE, "nq_fp8_gemm_backward: grad_format must be E4M3 or E5M2");
+    if (m == 0 || k == 0 || n == 0) return NQ_SUCCESS;
+    if (!grad_out || (grad_a && !b) || (grad_b && !a))
+        return nq::fail(NQ_ERROR_INVALID_VALUE, "nq_fp8_gemm_backward: null operand");
+    if (m > 65535 * 32 || k > 65535 * 32) return nq::fail(NQ_ERROR_UNSUPPORTED, "nq_fp8_gemm_backward: M or K too large");
+    nq_gemm_desc_t d;
+    std::memset(&d, 0, sizeof(d));
+    d.out_dtype = NQ_F32;
+    d.epilogue = NQ_EPI_NONE;
+    if (grad_a) {
+        // grad_a (M x K) = grad_out (M x N) . B^T: B (K x N row-major) is the N-by-K
+        // "packed" layout of the transposed operand
+        d.m = m; d.n = k; d.k = n;
+        d.a_format = grad_format; d.b_format = NQ_E4M3;
+        d.b_layout = NQ_B_NK;
+        d.alpha = scale_grad * scale_b;
+        nq_status_t st = nq::gemm_impl(&d, grad_out, b, grad_a, s, 0);
+        if (st != NQ_SUCCESS) return st;
+    }
+    if (grad_b) {
+        // grad_b (K x N) = A^T (K x M) . grad_out (M x N): A transposed once into
+        // pool scratch, grad_out read as a K x N (here M x N) row-major operand
+        void* at = nullptr;
+        nq_status_t st = nq::scratch_alloc(&at, static_cast<size_t>(m) * k, s);
+        if (st != NQ_SUCCESS) return st;
+        dim3 grid((k + 31) / 32, (m + 31) / 32);
+        nq::k_transpose_u8<<<grid, 256, 0, s>>>(a, static_cast<uint8_t*>(at), m, k);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            nq::scratch_free(at, s);
+            return nq::cuda_status(e, "nq_fp8_gemm_backward: transpose");
+        }
+        d.m = k; d.n = n; d.k = m;
+        d.a_format = NQ_E4M3; d.b_format = grad_format;
+        d.b_layout = NQ_B_KN;
+        d.alpha = scale_a * scale_grad;
+        st = nq::gemm_impl(&d, at, grad_out, grad_b, s, 0);
+        nq::scratch_free(at, s);
+        if (st != NQ_SUCCESS) return st;
+    }
+    return NQ_SUCCESS;
 }
 
 nq_status_t nq_mixed_precision_matmul(const float* a, const int8_t* b, const float* scale_b, float* out, int m, int k,

@@ -85,6 +85,15 @@ def test_gemm_allreduce_argument_checks_without_gpu():
     assert capi.allreduce_finish.raw(C.byref(ar), None) == 1                       # finish without a counter
 
 
+def test_fp8_backward_argument_checks_without_gpu():
+    import nova_b200.capi as capi
+    assert capi.fp8_gemm_backward.raw(16, 2, 16, 16, 16, 16, 4, 4, 4, 1.0, 1.0, 1.0, None) == 1   # INT8 grads
+    assert capi.fp8_gemm_backward.raw(16, 0, 16, 16, 16, 16, -1, 4, 4, 1.0, 1.0, 1.0, None) == 1  # negative size
+    assert capi.fp8_gemm_backward.raw(None, 0, 16, 16, 16, 16, 4, 4, 4, 1.0, 1.0, 1.0, None) == 1  # null grad
+    assert capi.fp8_gemm_backward.raw(16, 0, 16, None, 16, None, 4, 4, 4, 1.0, 1.0, 1.0, None) == 1  # grad_a needs B
+    assert capi.fp8_gemm_backward.raw(16, 0, 16, 16, 16, 16, 0, 4, 4, 1.0, 1.0, 1.0, None) == 0   # empty
+
+
 def test_no_device_is_an_error_not_a_crash():
     torch = pytest.importorskip("torch")
     if torch.cuda.is_available():

@@ -334,3 +334,30 @@ def test_swiglu_epilogue_rejects_unsupported(nq):
         desc = nq.make_desc(128, n, 128, fmt, fmt, 0, od, 1.0, epilogue=nq.EPI_SWIGLU)
         with pytest.raises(nq.NqError, match="UNSUPPORTED"):
             nq.gemm(desc, ptr(buf), ptr(buf), ptr(buf), stream())
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 512, 384), (200, 272, 176), (64, 128, 96), (33, 40, 24), (300, 1000, 130)])
+@pytest.mark.parametrize("gfmt", [0, 1])
+def test_fp8_backward_exact_vs_oracle(nq, m, k, n, gfmt):
+    """nq_fp8_gemm_backward: grad_a = g . B^T and grad_b = A^T . g (the
+    transposes FP8GEMM::backward omits), E4M3 operands, E4M3 or E5M2 gradient;
+    fp32 outputs against the oracle's accumulators on the transposed operands."""
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    a, sa = fp8_operand((m, k), 50 + m, 0)
+    b, sb = fp8_operand((k, n), 60 + n, 0)
+    g, sg = fp8_operand((m, n), 70 + k, gfmt)
+    d_a, d_b, d_g = dev(a), dev(b), dev(g)
+    d_ga, d_gb = empty(4 * m * k), empty(4 * k * n)
+    nq.fp8_gemm_backward(ptr(d_g), gfmt, ptr(d_a), ptr(d_b), ptr(d_ga), ptr(d_gb), m, k, n, sg, sa, sb, stream())
+    ga, gb = host(d_ga, np.float32, (m, k)), host(d_gb, np.float32, (k, n))
+    ref_ga = O.epilogue(O.gemm_fp8_acc(g, b, gfmt, 0, False), False, float(np.float32(sg) * np.float32(sb)))
+    ref_gb = O.epilogue(O.gemm_fp8_acc(np.ascontiguousarray(a.T), g, 0, gfmt, True), False,
+                        float(np.float32(sa) * np.float32(sg)))
+    assert rel_err(ga, ref_ga) <= FP8_TOL_F32_OBSERVED
+    assert rel_err(gb, ref_gb) <= FP8_TOL_F32_OBSERVED
+    # either gradient alone
+    d_ga2 = empty(4 * m * k)
+    nq.fp8_gemm_backward(ptr(d_g), gfmt, ptr(d_a), ptr(d_b), ptr(d_ga2), 0, m, k, n, sg, sa, sb, stream())
+    np.testing.assert_array_equal(host(d_ga2, np.float32, (m, k)), ga)
+    assert nq.device_error_flags() == 0
