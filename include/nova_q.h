@@ -99,6 +99,14 @@ nq_status_t nq_dequantize_int8_to_f32(const int8_t* src, float* dst, size_t n, f
 /* int8_kernels.hpp:75-79 (int8_kernels.cu:171-194) */
 nq_status_t nq_quantize_f32_to_int8_with_calibration(const float* src, int8_t* dst, size_t n,
                                                      float min_val, float max_val, nq_stream_t s);
+/* Element-wise activations on FP8 codes of the reference codec, the kernels of
+   include/cuda/quantize/fp8_activation.hpp (:26-59, :62-98): decode, activate
+   in fp32, re-encode (relu: negative inputs become +0, other codes pass
+   unchanged; gelu x*0.5*(1+erf(x/sqrt2)); sigmoid 1/(1+exp(-x)); leaky relu
+   x >= 0 ? x : alpha*x).  fmt NQ_E4M3 or NQ_E5M2. */
+typedef enum { NQ_ACT_RELU = 0, NQ_ACT_GELU = 1, NQ_ACT_SIGMOID = 2, NQ_ACT_LEAKY_RELU = 3 } nq_activation_t;
+nq_status_t nq_fp8_activation(const uint8_t* src, uint8_t* dst, size_t n, nq_format_t fmt,
+                              nq_activation_t op, float alpha, nq_stream_t s);
 /* FakeQuantize::forward of quantization-aware training (qat.hpp:64-72) over a
    device array: scale floored at 1e-6, q = clamp(round_half_away((x - zp) /
    scale), +-127), dst = q * scale + zp (multiply, then add). */

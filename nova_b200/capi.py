@@ -62,6 +62,7 @@ _SIGS = {
     "nq_quantize_f32_to_int8_with_calibration": [_p, _p, _sz, _f, _f, _p],
     "nq_quantize_f32_to_int8_round_away": [_p, _p, _sz, _f, _p],
     "nq_fake_quantize_int8": [_p, _p, _sz, _f, _f, _p],
+    "nq_fp8_activation": [_p, _p, _sz, _i, _i, _f, _p],
     "nq_compute_minmax": [_p, _sz, _p, _p, _p],
     "nq_build_histogram": [_p, _p, _sz, _f, _f, _i, _p],
     "nq_minmax_async": [_p, _sz, _p, _p],
@@ -126,6 +127,7 @@ def exported_symbols():
 
 
 EPI_NONE, EPI_SWIGLU = 0, 1
+ACT_RELU, ACT_GELU, ACT_SIGMOID, ACT_LEAKY_RELU = 0, 1, 2, 3
 
 
 def make_desc(m, n, k, a_format=E4M3, b_format=E4M3, b_layout=B_KN, out_dtype=BF16, alpha=1.0,

@@ -284,6 +284,49 @@ __global__ void __launch_bounds__(256) k_fake_quant(const float* __restrict__ sr
     for (size_t i = n4 * 4 + t0; i < n; i += stride) dst[i] = fake_quant1(__ldg(src + i), s, zp);
 }
 
+// Element-wise activations on FP8 codes of the reference codec
+// (fp8_activation.hpp:26-59 of pplmx/nova): decode, activate in fp32 with the
+// reference's expressions, re-encode; relu returns negative inputs as +0 and
+// every other input code unchanged.  16 codes per thread step.
+template <bool E4M3, int OP>
+__device__ __forceinline__ uint32_t fp8_act1(uint32_t c, float alpha) {
+    const float x = E4M3 ? dev::compat_e4m3_decode(c) : dev::compat_e5m2_decode(c);
+    float y;
+    if (OP == NQ_ACT_RELU) {
+        if (!(x < 0.0f)) return c;
+        y = 0.0f;
+    } else if (OP == NQ_ACT_GELU) {
+        const float cdf = 0.5f * (1.0f + erff(x * 0.7071067811865476f));
+        y = x * cdf;
+    } else if (OP == NQ_ACT_SIGMOID) {
+        y = 1.0f / (1.0f + expf(-x));
+    } else {
+        y = x >= 0.0f ? x : alpha * x;
+    }
+    return E4M3 ? dev::compat_e4m3_encode(y) : dev::compat_e5m2_encode(y);
+}
+template <bool E4M3, int OP>
+__global__ void __launch_bounds__(256) k_fp8_act(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, size_t n,
+                                                 int vec, float alpha) {
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t n16 = vec ? n / 16 : 0;
+    for (size_t v = t0; v < n16; v += stride) {
+        uint4 q = __ldg(reinterpret_cast<const uint4*>(src) + v);
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t o = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) o |= fp8_act1<E4M3, OP>((w[j] >> (8 * b)) & 0xFFu, alpha) << (8 * b);
+            w[j] = o;
+        }
+        reinterpret_cast<uint4*>(dst)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    for (size_t i = n16 * 16 + t0; i < n; i += stride)
+        dst[i] = static_cast<uint8_t>(fp8_act1<E4M3, OP>(__ldg(src + i), alpha));
+}
+
 // ---- launch helpers ------------------------------------------------------------------
 nq_status_t grid_for(size_t n, int* grid) {
     DeviceInfo di;
@@ -427,6 +470,37 @@ nq_status_t nq_quantize_f32_to_int8_round_away(const float* src, int8_t* dst, si
                                                nq_stream_t s) {
     return nq::launch_quant(src, reinterpret_cast<uint8_t*>(dst), n, nq::Int8RoundAway{scale}, s,
                             "nq_quantize_f32_to_int8_round_away");
+}
+
+nq_status_t nq_fp8_activation(const uint8_t* src, uint8_t* dst, size_t n, nq_format_t fmt, nq_activation_t op,
+                              float alpha, nq_stream_t s) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst) return fail(NQ_ERROR_INVALID_VALUE, "nq_fp8_activation: null pointer");
+    if (fmt != NQ_E4M3 && fmt != NQ_E5M2) return fail(NQ_ERROR_INVALID_VALUE, "nq_fp8_activation: format");
+    if (op < NQ_ACT_RELU || op > NQ_ACT_LEAKY_RELU) return fail(NQ_ERROR_INVALID_VALUE, "nq_fp8_activation: op");
+    int grid;
+    nq_status_t st = nq::grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    const int vec = nq::aligned16(src) && nq::aligned16(dst);
+#define NQ_ACT(E, OP) nq::k_fp8_act<E, OP><<<grid, 256, 0, s>>>(src, dst, n, vec, alpha)
+    if (fmt == NQ_E4M3) {
+        switch (op) {
+            case NQ_ACT_RELU: NQ_ACT(true, NQ_ACT_RELU); break;
+            case NQ_ACT_GELU: NQ_ACT(true, NQ_ACT_GELU); break;
+            case NQ_ACT_SIGMOID: NQ_ACT(true, NQ_ACT_SIGMOID); break;
+            default: NQ_ACT(true, NQ_ACT_LEAKY_RELU); break;
+        }
+    } else {
+        switch (op) {
+            case NQ_ACT_RELU: NQ_ACT(false, NQ_ACT_RELU); break;
+            case NQ_ACT_GELU: NQ_ACT(false, NQ_ACT_GELU); break;
+            case NQ_ACT_SIGMOID: NQ_ACT(false, NQ_ACT_SIGMOID); break;
+            default: NQ_ACT(false, NQ_ACT_LEAKY_RELU); break;
+        }
+    }
+#undef NQ_ACT
+    NQ_LAUNCH_CHECK("nq_fp8_activation");
+    return NQ_SUCCESS;
 }
 
 nq_status_t nq_fake_quantize_int8(const float* src, float* dst, size_t n, float scale, float zero_point,

@@ -623,3 +623,29 @@ void orc_fake_quantize_int8(const float* src, float* dst, size_t n, float scale,
         dst[i] = m + zero_point;
     }
 }
+
+/* FP8 activations of fp8_activation.hpp:26-59 on reference-codec codes: decode,
+   activate in fp32 (libm erff / expf), re-encode; relu keeps non-negative
+   codes (and NaN codes) unchanged and maps negative ones to +0.
+   op 0 relu, 1 gelu, 2 sigmoid, 3 leaky relu; fmt 0 E4M3, 1 E5M2. */
+void orc_fp8_activation(const uint8_t* src, uint8_t* dst, size_t n, int fmt, int op, float alpha) {
+    for (size_t i = 0; i < n; ++i) {
+        const float x = fmt == 0 ? orc_e4m3_compat_decode(src[i]) : orc_e5m2_compat_decode(src[i]);
+        float y;
+        if (op == 0) {
+            if (!(x < 0.0f)) {
+                dst[i] = src[i];
+                continue;
+            }
+            y = 0.0f;
+        } else if (op == 1) {
+            const float cdf = 0.5f * (1.0f + erff(x * 0.7071067811865476f));
+            y = x * cdf;
+        } else if (op == 2) {
+            y = 1.0f / (1.0f + expf(-x));
+        } else {
+            y = x >= 0.0f ? x : alpha * x;
+        }
+        dst[i] = fmt == 0 ? orc_e4m3_compat_encode(y) : orc_e5m2_compat_encode(y);
+    }
+}

@@ -117,6 +117,9 @@ float orc_silu_mul(float g, float u);
 void orc_swiglu_epilogue(const float* acc, void* out, int out_bf16, int m, int n, float alpha,
                          const float* row_scale, const float* col_scale, const float* bias);
 
+/* FP8 activations on reference-codec codes (fp8_activation.hpp:26-59):
+   op 0 relu, 1 gelu, 2 sigmoid, 3 leaky relu (alpha); fmt 0 E4M3, 1 E5M2 */
+void orc_fp8_activation(const uint8_t* src, uint8_t* dst, size_t n, int fmt, int op, float alpha);
 /* QAT FakeQuantize::forward over an array (qat.hpp:64-72) */
 void orc_fake_quantize_int8(const float* src, float* dst, size_t n, float scale, float zero_point);
 

@@ -49,6 +49,7 @@ for name, res, args in [
     ("orc_swiglu_epilogue", None, [_p, _p, _i, _i, _i, _f, _p, _p, _p]),
     ("orc_silu_mul", _f, [_f, _f]),
     ("orc_fake_quantize_int8", None, [_p, _p, _sz, _f, _f]),
+    ("orc_fp8_activation", None, [_p, _p, _sz, _i, _i, _f]),
 ]:
     fn = getattr(lib, name)
     fn.restype = res
@@ -306,3 +307,10 @@ def fake_quantize(x, scale, zero_point):
     y = np.empty_like(x)
     lib.orc_fake_quantize_int8(ptr(x), ptr(y), x.size, scale, zero_point)
     return y
+
+
+def fp8_activation(codes, fmt, op, alpha=0.01):
+    codes = np.ascontiguousarray(codes, np.uint8)
+    out = np.empty_like(codes)
+    lib.orc_fp8_activation(ptr(codes), ptr(out), codes.size, fmt, op, alpha)
+    return out

@@ -225,3 +225,31 @@ def test_fake_quantize_reference_golden(nq):
         d_x, d_y = dev(x), empty(4 * x.size)
         nq.fake_quantize_int8(ptr(d_x), ptr(d_y), x.size, float(scale), float(zp), stream())
         np.testing.assert_array_equal(host(d_y, np.float32).view(np.uint32), y.view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+def test_fp8_activation_vs_oracle(nq, fmt, op):
+    """FP8 activations on reference-codec codes (nq_fp8_activation,
+    fp8_activation.hpp:26-98): every code, plus a long random array through
+    the 16-code vector path, its tail and an unaligned pointer.  relu and leaky
+    relu are bit-exact; gelu and sigmoid use CUDA's erff / expf against the
+    host libm of the oracle, so a code may differ by one step where the fp32
+    result sits within a few ulp of a rounding boundary (at most 1 in 256)."""
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    rng = np.random.default_rng(11 + op)
+    for codes, off in [(np.arange(256, dtype=np.uint8), 0),
+                       (rng.integers(0, 256, (1 << 20) + 7, dtype=np.uint8), 0),
+                       (rng.integers(0, 256, 1000, dtype=np.uint8), 3)]:
+        d_x, d_y = dev(codes, off), empty(codes.size, off)
+        nq.fp8_activation(ptr(d_x), ptr(d_y), codes.size, fmt, op, 0.01, stream())
+        got = host(d_y, np.uint8)
+        ref = O.fp8_activation(codes, fmt, op, 0.01)
+        diff = got != ref
+        if op in (0, 3):
+            assert not diff.any()
+        else:
+            assert diff.mean() <= 1 / 256
+            assert (np.abs(got[diff].astype(int) - ref[diff].astype(int)) <= 1).all()
+    assert nq.device_error_flags() == 0
