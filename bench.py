@@ -302,8 +302,13 @@ def run_ours(args):
     torch.cuda.empty_cache()
     tp_res = None
     if not args.no_tp_mlp:
-        tp_res = tp_mlp_bench(world, rank, max(3, min(args.steps, 10)), args.warmup if args.warmup < 5 else 5,
-                              chunks=args.tp_chunks, overlap=args.tp_overlap, allreduce=args.tp_allreduce)
+        # a failure of the secondary TP block must not cost the headline line
+        try:
+            tp_res = tp_mlp_bench(world, rank, max(3, min(args.steps, 10)), args.warmup if args.warmup < 5 else 5,
+                                  chunks=args.tp_chunks, overlap=args.tp_overlap, allreduce=args.tp_allreduce)
+        except Exception as e:  # reported in the JSON line instead
+            tp_res = {"error": f"{type(e).__name__}: {e}"[:300]}
+            torch.cuda.synchronize()
 
     if rank != 0:
         if world > 1:
