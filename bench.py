@@ -341,7 +341,11 @@ def run_ours(args):
                                                   torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda"))
     if not args.no_secondary:
         sizes = tuple(int(v) for v in args.sweep_sizes.split(","))
-        line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps), **c3_c4_bench(pk)}
+        try:
+            line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps),
+                                 **c3_c4_bench(pk)}
+        except Exception as e:  # reported, the headline line still prints
+            line["secondary"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
