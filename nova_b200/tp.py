@@ -150,7 +150,10 @@ class SymmetricAllReduce:
         on first use.  Counters are zeroed on every rank before any rank can
         signal (a barrier follows the clear).  States live as long as the
         layer: peers may still be reading a buffer when this rank moves to
-        another shape."""
+        another shape.  Each new token count therefore costs one collective
+        allocation and 4 * m * n bytes of symmetric memory kept until the
+        layer is dropped: callers with many distinct token counts should pad
+        them to a few sizes."""
         key = (m, n, tuple(bounds))
         if key not in self._states:
             t, nq = self.torch, self.nq
