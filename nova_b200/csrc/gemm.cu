@@ -1,18 +1,19 @@
 // gemm.cu -- FP8 (kind::f8f6f4) and INT8 (kind::i8) GEMMs on the sm_100a
-// tensor cores, with the scale / bias / bf16 epilogue fused.
+// tensor cores, with the scale / bias / bf16 / int8 / SwiGLU epilogues fused,
+// and the GEMM-fused all-reduce of a row-parallel layer.
 //
-// Kernel k_gemm_tc (persistent, one CTA per SM, 192 threads):
-//   warp 0      TMA producer: A tile [128 x 128 B] and B tile [128 B x 256]
-//               per stage, 128-byte swizzle, 4-stage ring of 48 KB stages.
-//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32/s32
-//               accumulators) and one elected thread issues tcgen05.mma
-//               (M=128, N=256, K=32 per instruction, 4 per stage), committing
-//               each stage back to the producer and each finished tile to the
-//               epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output rows),
-//               acc * alpha [* row_scale] [* col_scale] [+ bias], convert,
-//               store; then hand the accumulator back, so the MMA of tile i+1
-//               overlaps the epilogue of tile i.
+// Kernel k_gemm_tc2 (M > 128, and every SwiGLU / all-reduce GEMM): a cluster
+//   of two CTAs computes 256 x 256 tiles with tcgen05.mma.cta_group::2; warp 0
+//   of each CTA loads its half of A and B by TMA (5-stage ring), warp 1 of the
+//   first CTA issues the MMAs, warps 2..9 of both CTAs drain TMEM through the
+//   epilogue and TMA stores; persistent grid, banded tile order.  The AR
+//   variant adds reducer warps (ar_job) and a signaller (ar_signal_tiles).
+// Kernel k_gemm_tc (M <= 128; persistent, one CTA per SM, 192 threads):
+//   warp 0 TMA producer ([128 x 128 B] A and [128 B x 256] B per stage,
+//   4-stage ring), warp 1 MMA issuer (M=128, N=256), warps 2..5 epilogue.
+// Kernel k_gemm_decode (M <= 32 against large weights): operands swapped so
+//   128 weight rows are the MMA's M side, stream-K over weight slices with a
+//   deterministic fixup.
 // B is read either K x N row-major (FP8GEMM::forward's layout, the MN-major
 // operand form of tcgen05) or N x K row-major (K-major, a packed weight).
 // Every wait is bounded (ptx.cuh); a timeout sets the device error word.
