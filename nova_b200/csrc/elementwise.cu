@@ -4,7 +4,8 @@
 // stores: one thread handles 16 elements per step (64 B of fp32 in and 16 B
 // of codes out for a quantize), on a grid-stride loop over a grid sized to the
 // SM count.  Tails (n % 16) and unaligned pointers take a scalar loop with the
-// same arithmetic, so the result never depends on the path.
+// same arithmetic, so the result never depends on the path.  Also here: QAT
+// fake quantize (fp32 -> fp32) and the activations on FP8 codes.
 #include <algorithm>
 
 #include "codec.cuh"

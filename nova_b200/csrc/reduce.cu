@@ -6,6 +6,10 @@
 // stream-ordered scratch, and the last block to arrive (atomic ticket) folds the
 // partials and writes the result to device memory -- no host round trip, unlike
 // the reference's host-side finish (int8_kernels.cu:379-389).
+//
+// Per-row quantize stages whole rows in shared memory with 1-D bulk copies:
+// one warp per row up to 12 KB (k_quant_rows_warp), one block per row up to
+// 100 KB (k_quant_rows_bulk), a two-pass kernel otherwise (k_quant_rows).
 #include <algorithm>
 #include <cfloat>
 #include <cstring>
