@@ -10,19 +10,23 @@ output.  Here the layers are W8A8 FP8 on the tcgen05 GEMMs of libnova_q:
   x (bf16, replicated)   -> per-token FP8 quantize          nq_quantize_rows
   [Wg|Wu] column shards  -> one GEMM, fused silu(g)*u       nq_gemm + NQ_EPI_SWIGLU
   h (bf16, this shard)   -> per-token FP8 quantize          nq_quantize_rows
-  Wd row shard           -> partial output (bf16)           nq_gemm
-  partial                -> sum over ranks (bf16 NCCL all-reduce through
-                            torch.distributed, chunked along the tokens so
-                            the down-projection of chunk i+1 overlaps the
-                            all-reduce of chunk i)
+  Wd row shard           -> partial output + all-reduce     nq_gemm_allreduce
+
+The all-reduce runs inside the GEMM kernels over NVLink (allreduce "auto":
+NVSwitch multicast when present, else peer memory): the down GEMM of a token
+chunk writes this rank's partial tiles and signals their owners; the chunk's
+reduction runs in the reducer warps of the next chunk's gate/up GEMM, and the
+last down GEMM reduces its own chunk and waits for completion.  allreduce
+"nccl" keeps a chunked torch.distributed all_reduce instead.
 
 Weights are per-output-channel FP8 E4M3 (scale = column amax / 448, computed
 on each rank's shard).  Shard layouts follow the reference set_weight
 (column shard: columns [r*N/tp, (r+1)*N/tp) of a row-major K x N weight,
 tensor_parallel_layers.cpp:111-136; row shard: rows [r*K/tp, ...), :344-368).
 The reference takes an NcclContext; these classes take a torch.distributed
-process group (NCCL on GPUs), whose size is the TP degree.  Streams, device
-memory and the collective come from PyTorch; all arithmetic runs in libnova_q.
+process group (NCCL on GPUs), whose size is the TP degree.  Rendezvous,
+symmetric memory mappings, streams and device memory come from PyTorch; all
+arithmetic and the all-reduce run in libnova_q.
 """
 from __future__ import annotations
 
