@@ -10,11 +10,17 @@ reference's K x N layout (FP8GEMM::forward).  One step = one GEMM launch.
 
 N > 1 (torchrun): every rank runs the same GEMM on its own GPU (replicas, no
 collective on the data path); value = all ranks' FLOPs / max-over-ranks time.
-The "tp_mlp" block times BASELINE configs[4], the tensor-parallel FP8 SwiGLU
-MLP, with tp = N (strong scaling, T = 16384 tokens at every N, bf16 NCCL
-all-reduce of the row-parallel output).
+
+Output: rank 0 prints the secondary workloads (quantize bandwidth sweep, C3,
+C4) on a line of their own starting with "secondary ", then ONE JSON line
+whose last key, "tp_mlp", times BASELINE configs[4] -- the tensor-parallel
+FP8 SwiGLU MLP with tp = N (strong scaling, T = 16384 tokens at every N,
+GEMM-fused bf16 all-reduce of the row-parallel output) -- with a parity check
+of sampled output rows and, for N > 1, the tp = 1 time measured in the same
+run on every GPU.
 --impl reference times the reference algorithm on the host cores (the CPU
-oracle port of FP8GEMM::forward's naive kernel, fp8_gemm.cu:64-86), rank 0 only.
+oracle port of FP8GEMM::forward's naive kernel, fp8_gemm.cu:64-86, on all
+host threads), rank 0 only, plus the reference's own host code on one core.
 """
 from __future__ import annotations
 
@@ -170,6 +176,83 @@ def make_operands(seed_a=2, seed_b=3):
     return out
 
 
+def ref_host_lib():
+    """The reference's own host code (pplmx/nova's fp8_types.hpp,
+    quantize_tensor.hpp and quantize_ops.hpp compiled from the reference tree
+    into oracle/_ref/libnova_ref_host.so by oracle/Makefile), or None."""
+    import ctypes as C
+    path = os.path.join(ROOT, "oracle", "_ref", "libnova_ref_host.so")
+    if not os.path.exists(path):
+        return None
+    lib = C.CDLL(path)
+    lib.ref_e4m3_encode_array.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
+    lib.ref_e4m3_encode_array.restype = None
+    lib.ref_from_float_int8.argtypes = [C.c_void_p, C.c_size_t, C.c_float, C.c_void_p, C.c_void_p]
+    lib.ref_from_float_int8.restype = C.c_int
+    lib.ref_quantized_matmul.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float,
+                                         C.c_float]
+    lib.ref_quantized_matmul.restype = None
+    return lib
+
+
+def cpu_reference_host():
+    """Times the reference's OWN host code on one core (single-threaded by
+    construction): FP8E4M3(float) over an array (fp8_types.hpp:64-97, the loop
+    of benchmark_fp8_roundtrip, benchmark.cpp:308-335),
+    QuantizedTensor<int8_t>::FromFloat (quantize_tensor.hpp:160-191: amax and
+    round-half-away quantize) and QuantizedMatmul::forward
+    (quantize_ops.hpp:54-81) at the C1 shape and on row slices of the C4
+    decode shape (scaled linearly to M = 16).  Bytes per element as the GPU
+    kernels count them: quantize 5 B (4 read + 1 write); C4 K*N + M*K + 2*M*N
+    + 4*(M+N)."""
+    import ctypes as C
+    import numpy as np
+    lib = ref_host_lib()
+    if lib is None:
+        return {"unavailable": "oracle/_ref/libnova_ref_host.so not built (needs the pplmx/nova source tree)"}
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    rng = np.random.default_rng(13)
+    res = []
+    for n in (1 << 20, 56 << 20):
+        x = rng.standard_normal(n, dtype=np.float32)
+        q = np.empty(n, np.uint8)
+        t0 = time.perf_counter()
+        lib.ref_e4m3_encode_array(vp(x), vp(q), n)
+        dt = time.perf_counter() - t0
+        res.append({"code": "FP8E4M3(float) array encode", "n": n, "s": round(dt, 4),
+                    "GB/s": round(5.0 * n / dt / 1e9, 3), "Melem/s": round(n / dt / 1e6, 1)})
+        qi = np.empty(n, np.int8)
+        sc = np.zeros(1, np.float32)
+        t0 = time.perf_counter()
+        lib.ref_from_float_int8(vp(x), n, 0.0, vp(qi), vp(sc))
+        dt = time.perf_counter() - t0
+        res.append({"code": "QuantizedTensor<int8_t>::FromFloat (amax + quantize)", "n": n, "s": round(dt, 4),
+                    "GB/s": round(5.0 * n / dt / 1e9, 3), "Melem/s": round(n / dt / 1e6, 1)})
+        del x, q, qi
+    m, k, n = 128, 1024, 1024                                     # BASELINE configs[0]
+    a = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    b = rng.integers(-127, 128, (k, n), dtype=np.int8)
+    o = np.empty((m, n), np.int8)
+    t0 = time.perf_counter()
+    lib.ref_quantized_matmul(vp(a), vp(b), vp(o), m, k, n, 0.01, 0.01)
+    dt = time.perf_counter() - t0
+    res.append({"code": "QuantizedMatmul::forward", "shape": [m, k, n], "s": round(dt, 4),
+                "GOP/s": round(2.0 * m * k * n / dt / 1e9, 3)})
+    kd, nd, rows = 8192, 28672, 1                                 # BASELINE configs[3], M = 16 scaled from 1 row
+    a = rng.integers(-127, 128, (rows, kd), dtype=np.int8)
+    b = rng.integers(-127, 128, (kd, nd), dtype=np.int8)
+    o = np.empty((rows, nd), np.int8)
+    t0 = time.perf_counter()
+    lib.ref_quantized_matmul(vp(a), vp(b), vp(o), rows, kd, nd, 0.01, 0.01)
+    dt = time.perf_counter() - t0
+    t16 = dt * 16 / rows
+    c4_bytes = kd * nd + 16 * kd + 2 * 16 * nd + 4 * (16 + nd)
+    res.append({"code": "QuantizedMatmul::forward", "shape": [16, kd, nd], "sample_rows": rows,
+                "s_scaled_to_m16": round(t16, 3), "GB/s": round(c4_bytes / t16 / 1e9, 4),
+                "GOP/s": round(2.0 * 16 * kd * nd / t16 / 1e9, 3)})
+    return {"cores": 1, "kind": "reference", "host_nproc": os.cpu_count(), "results": res}
+
+
 def cpu_reference_sample(rows, threads):
     """Times the oracle port of the reference FP8 GEMM (naive kernel order,
     compat decode, fp32 FMA) on `rows` rows of the 4096^3 problem."""
@@ -188,14 +271,19 @@ def cpu_reference_sample(rows, threads):
 
 
 def cpu_baseline(target_s=8.0):
-    threads = os.cpu_count() or 1
-    dt, used = cpu_reference_sample(max(1, threads), threads)     # calibration
-    rate = (2.0 * max(1, threads) * N * K) / dt
-    rows = int(max(threads, min(M, target_s * rate / (2.0 * N * K))))
-    dt, used = cpu_reference_sample(rows, threads)
+    """The headline metric on ONE host core: the oracle port of the
+    reference's FP8GEMM::forward (its naive kernel's order, decode and FMA,
+    fp8_gemm.cu:64-86; the reference has no host FP8 GEMM of its own) on a
+    row slice of the 4096^3 problem, plus the reference's own host code
+    (cpu_reference_host) for the quantize and INT8 GEMM paths."""
+    dt, used = cpu_reference_sample(4, 1)                       # calibration
+    rate = (2.0 * 4 * N * K) / dt
+    rows = int(max(4, min(M, target_s * rate / (2.0 * N * K))))
+    dt, used = cpu_reference_sample(rows, 1)
     tflops = 2.0 * rows * N * K / dt / 1e12
     return {"value": tflops, "unit": "TFLOP/s", "cores": used, "kind": "port",
-            "sample": f"{rows} of 4096 rows of the 4096^3 FP8 GEMM (naive reference order), {dt:.1f} s"}
+            "sample": f"{rows} of 4096 rows of the 4096^3 FP8 GEMM (naive reference order, 1 thread), {dt:.1f} s",
+            "reference_host_code": cpu_reference_host()}
 
 
 def run_reference(args):
@@ -221,7 +309,8 @@ def run_reference(args):
         "config": {"workload": "fp8_gemm_4096 (BASELINE configs[1]), host sample", "m": M, "n": N, "k": K,
                    "rows_per_step": rows},
         "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": used, "kind": "port",
-                         "sample": f"{rows} of 4096 rows per step (oracle port of fp8_gemm.cu:64-86)"},
+                         "sample": f"{rows} of 4096 rows per step (oracle port of fp8_gemm.cu:64-86)",
+                         "reference_host_code": cpu_reference_host()},
         "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -334,20 +423,22 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
-    if tp_res is not None:
-        line["tp_mlp"] = tp_res
     if args.cublas:
         line["library_comparison"] = cublaslt_fp8(args.steps, args.warmup,
                                                   torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda"))
     if not args.no_secondary:
+        # printed on a line of its own before the result line, which it would
+        # otherwise push out of the tail of the log a reader keeps
         sizes = tuple(int(v) for v in args.sweep_sizes.split(","))
         try:
-            line["secondary"] = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps),
-                                 **c3_c4_bench(pk)}
+            sec = {"quantize_hbm": quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps), **c3_c4_bench(pk)}
         except Exception as e:  # reported, the headline line still prints
-            line["secondary"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            sec = {"error": f"{type(e).__name__}: {e}"[:300]}
+        print("secondary " + json.dumps(sec), flush=True)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
+    if tp_res is not None:
+        line["tp_mlp"] = tp_res          # last key: the sharded workload closes the line
     print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -487,31 +578,9 @@ def c3_c4_bench(pk, reps=20):
     return res
 
 
-def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=None, overlap="full", allreduce="auto"):
-    """BASELINE configs[4]: the FP8 SwiGLU MLP (nova_b200.tp.TensorParallelMLP)
-    with tp = world size, T tokens per step (strong scaling: the same T at
-    every tp).  x ~ N(0,1) bf16, weights ~ N(0,0.02) fp32 generated on the
-    device from fixed seeds (identical on every rank), sharded and FP8
-    quantized by set_weight.  One step = forward() (per-token quantize,
-    gate/up GEMM + SwiGLU, quantize, down GEMM, chunked bf16 NCCL
-    all-reduce); time = max over ranks of the CUDA-event time of `steps`
-    forwards.  Inputs (256 MiB) and weights exceed L2.  allreduce "auto" /
-    "nvls" / "p2p": the down GEMM and the all-reduce are one kernel
-    (nq_gemm_allreduce) and forward returns the symmetric output buffer;
-    "nccl": chunked GEMM + torch.distributed all_reduce into `out`."""
+def _time_mlp(mlp, x, out, T, steps, warmup, world):
+    """max-over-ranks CUDA-event ms per forward of `steps` forwards."""
     import torch
-    from nova_b200.tp import TensorParallelMLP
-    g = torch.Generator(device="cuda").manual_seed(11)
-    mlp = TensorParallelMLP(H, I, chunks=chunks, overlap=overlap, allreduce=allreduce)
-    wg = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
-    wu = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
-    wd = torch.randn(I, H, device="cuda", generator=g).mul_(0.02)
-    mlp.set_weight(wg, wu, wd)
-    del wg, wu, wd
-    torch.cuda.empty_cache()
-    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
-    fused = mlp.down.fused is not None
-    out = None if fused else torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     for _ in range(max(warmup, 5)):
         mlp.forward(x, out, 1, T, sync=False)
     torch.cuda.synchronize()
@@ -524,7 +593,129 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=No
         mlp.forward(x, out, 1, T, sync=False)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    return max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+
+def tp_parity(mlp, x, y, shards, rows, world, group=None):
+    """Parity of sampled output rows of the TP MLP, every rank taking part.
+
+    (a) From the GPU's own FP8 codes and scales: the per-token codes of x and
+        of h are re-derived in torch from x and from the GPU's h (bit-exact:
+        same multiply by qmax/amax, RNE E4M3); the accumulators are fp64 sums
+        of the exactly decoded codes.  h within 1e-2 (max relative error,
+        |ref| floored at 1e-2 rms); the output within 1e-2 of the sum over
+        ranks of the bf16 partials computed from the GPU's own h, relative to
+        sum_r |partial_r| (floored at 1e-2 of its rms) -- the bars of
+        tests/test_tp_gpu.py.
+    (b) Against an fp32 computation with the UNQUANTIZED weights
+        (tensor_parallel_layers.cpp:561-579 in fp32): normwise relative error,
+        bounded by 0.1 (two FP8 E4M3 quantizations of activations and weights
+        cost about 2^-4/sqrt(3) relative noise each).
+    Also: every rank's sampled output rows bit-identical (replicated) and the
+    device error word clear on every rank."""
+    import torch
+    import torch.distributed as dist
+    import nova_b200.capi as nq
+    f8 = torch.float8_e4m3fn
+    T = x.shape[0]
+    idx = torch.tensor(rows, device="cuda")
+
+    def token_codes(v):
+        """nq_quantize_rows' arithmetic on fp32 rows: (codes, scales)."""
+        amax = v.abs().amax(dim=1)
+        scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+        inv = torch.where(amax > 0, 448.0 / amax, torch.ones_like(amax))
+        ok = torch.isfinite(inv)
+        q = torch.where(ok[:, None], v * inv[:, None], v / scale[:, None])
+        return q.to(f8), scale
+
+    def rel(got, ref):
+        floor = 1e-2 * torch.sqrt(torch.mean(ref * ref)) + 1e-30
+        return float(torch.max(torch.abs(got - ref) / torch.maximum(torch.abs(ref), floor)))
+
+    gu, dl = mlp.gate_up, mlp.down.lin
+    xq, sx = gu._ws[T]
+    hq, sh = dl._ws[T]
+    h_gpu = mlp._h[T][idx].double()
+    xr = x[idx].float()
+    xc, xs = token_codes(xr)
+    codes_x_ok = torch.equal(xc.view(torch.uint8), xq[idx]) and torch.equal(xs, sx[idx])
+    # gate/up: packed [g_0 | u_0 | g_1 | ...] blocks of 128 columns
+    acc = xq[idx].view(f8).double() @ gu.q.view(f8).double()
+    gv = acc * sx[idx].double()[:, None] * gu.s.double()[None, :]
+    gv = gv.view(len(rows), -1, 2, 128)
+    g, u = gv[:, :, 0, :].reshape(len(rows), -1), gv[:, :, 1, :].reshape(len(rows), -1)
+    h_ref = (g / (1.0 + torch.exp(-g))) * u
+    h_err = rel(h_gpu, h_ref)
+    hc, hs = token_codes(mlp._h[T][idx].float())
+    codes_h_ok = torch.equal(hc.view(torch.uint8), hq[idx]) and torch.equal(hs, sh[idx])
+    part = (hq[idx].view(f8).double() @ dl.q.view(f8).double()) * sh[idx].double()[:, None] * dl.s.double()[None, :]
+    part = part.to(torch.bfloat16).double()
+    mag = part.abs()
+    if world > 1:
+        dist.all_reduce(part, group=group)
+        dist.all_reduce(mag, group=group)
+    got = y[idx].double()
+    floor = 1e-2 * torch.sqrt(torch.mean(mag * mag)) + 1e-30
+    out_err = float(torch.max(torch.abs(got - part) / torch.maximum(mag, floor)))
+    # (b) fp32 with the unquantized weight shards
+    wg, wu, wd = shards
+    xf = x[idx].float()
+    gf, uf = xf @ wg, xf @ wu
+    p32 = ((gf / (1.0 + torch.exp(-gf))) * uf) @ wd
+    if world > 1:
+        dist.all_reduce(p32, group=group)
+    fp32_norm = float(torch.linalg.norm(got - p32.double()) / torch.linalg.norm(p32.double()))
+    # replicated output and device errors on every rank
+    mx, mn = y[idx].float().clone(), y[idx].float().clone()
+    flags = torch.tensor([float(nq.device_error_flags()), 0.0 if (codes_x_ok and codes_h_ok) else 1.0],
+                         device="cuda")
+    if world > 1:
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN, group=group)
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=group)
+        errs = torch.tensor([h_err], device="cuda", dtype=torch.float64)
+        dist.all_reduce(errs, op=dist.ReduceOp.MAX, group=group)
+        h_err = float(errs.item())
+    replicated = bool(torch.equal(mx, mn))
+    dev_err = int(flags[0].item())
+    codes_ok = flags[1].item() == 0.0
+    ok = (h_err <= 1e-2 and out_err <= 1e-2 and fp32_norm <= 0.1 and replicated and dev_err == 0 and codes_ok)
+    return {"ok": ok, "rows": len(rows), "codes_bit_exact": codes_ok, "h_max_rel_err": round(h_err, 6),
+            "out_max_rel_err": round(out_err, 6), "vs_fp32_weights_norm_err": round(fp32_norm, 5),
+            "replicated": replicated, "device_errors": dev_err}
+
+
+def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=None, overlap="full", allreduce="auto",
+                 parity_rows=64):
+    """BASELINE configs[4]: the FP8 SwiGLU MLP (nova_b200.tp.TensorParallelMLP)
+    with tp = world size, T tokens per step (strong scaling: the same T at
+    every tp).  x ~ N(0,1) bf16, weights ~ N(0,0.02) fp32 generated on the
+    device from fixed seeds (identical on every rank), sharded and FP8
+    quantized by set_weight.  One step = forward() (per-token quantize,
+    gate/up GEMM + SwiGLU, quantize, down GEMM, all-reduce); time = max over
+    ranks of the CUDA-event time of `steps` forwards.  Inputs (256 MiB) and
+    weights exceed L2.  allreduce "auto" / "nvls" / "p2p": the down GEMM and
+    the all-reduce are one kernel (nq_gemm_allreduce) and forward returns the
+    symmetric output buffer; "nccl": chunked GEMM + torch.distributed
+    all_reduce into `out`.  With tp > 1, every GPU then also runs the whole
+    MLP alone (tp = 1, a one-rank group each, all GPUs at once) for the
+    strong-scaling reference measured in the same run."""
+    import torch
+    import torch.distributed as dist
+    from nova_b200.tp import TensorParallelMLP, shard_columns, shard_rows
+    g = torch.Generator(device="cuda").manual_seed(11)
+    mlp = TensorParallelMLP(H, I, chunks=chunks, overlap=overlap, allreduce=allreduce)
+    wg = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
+    wu = torch.randn(H, I, device="cuda", generator=g).mul_(0.02)
+    wd = torch.randn(I, H, device="cuda", generator=g).mul_(0.02)
+    mlp.set_weight(wg, wu, wd)
+    shards = (shard_columns(wg, rank, world).contiguous(), shard_columns(wu, rank, world).contiguous(),
+              shard_rows(wd, rank, world).contiguous())
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    fused = mlp.down.fused is not None
+    out = None if fused else torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    ms = _time_mlp(mlp, x, out, T, steps, warmup, world)
     flops = 6.0 * T * H * I
     pk = peaks()
     fp8_peak = 2.0 * pk["bf16_tflops"]
@@ -532,11 +723,29 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=No
     res = {"workload": "tp_fp8_swiglu_mlp (BASELINE configs[4])", "tokens": T, "hidden": H, "intermediate": I,
            "tp": world, "allreduce": (("fused-nvls" if mlp.down.fused.multicast() else "fused-p2p") if fused
                                       else ("nccl" if world > 1 else "none")),
-           "chunks": mlp.chunks, "overlap": overlap if not fused else "fused", "ms_per_step": round(ms, 4),
-           "tokens_per_s": T / (ms * 1e-3), "tflops_total": tflops,
-           "frac_of_tp_x_fp8_peak": tflops / (world * fp8_peak),
+           "chunks": mlp.chunks, "ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3)),
+           "tflops_total": round(tflops, 1), "frac_of_tp_x_fp8_peak": round(tflops / (world * fp8_peak), 4),
            "allreduce_bytes": 2 * T * H if world > 1 else 0, "scaling": "strong"}
-    del mlp, x, out
+    # parity of sampled rows spread over every token chunk, from one more forward
+    y = mlp.forward(x, out, 1, T, sync=True)
+    rows = sorted(set(int(v) for v in torch.linspace(0, T - 1, parity_rows).round().tolist()))
+    try:
+        res["parity"] = tp_parity(mlp, x, y, shards, rows, world)
+    except Exception as e:  # reported in the line
+        res["parity"] = {"ok": False, "error": f"{type(e).__name__}: {e}"[:200]}
+    del mlp, out, y, shards
+    torch.cuda.empty_cache()
+    if world > 1:
+        # tp = 1 on every GPU at once (one-rank groups), same inputs and weights
+        groups = [dist.new_group([r]) for r in range(world)]
+        solo = TensorParallelMLP(H, I, group=groups[rank])
+        solo.set_weight(wg, wu, wd)
+        o1 = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        ms1 = _time_mlp(solo, x, o1, T, steps, warmup, world)
+        res["tp1_ms_per_step_same_run"] = round(ms1, 4)
+        res["strong_scaling_vs_tp1"] = round(ms1 / (world * ms), 4)
+        del solo, o1
+    del wg, wu, wd, x
     torch.cuda.empty_cache()
     return res
 

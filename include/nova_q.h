@@ -66,6 +66,14 @@ int nq_version(void);
 /* Reads (and with clear != 0 resets) the device-side error word of the
    current device: bit 0 = a bounded wait in a kernel timed out. */
 nq_status_t nq_device_error_flags(uint32_t* flags, int clear);
+/* Upper bound, in ns, of a kernel's wait on counts sent by other GPUs (the
+   fused all-reduce below; default 5 s, 0 restores the default).  Applies to
+   kernels launched after the call, process-wide.  A wait that runs out sets
+   bit 0 of the device error word and the kernel returns.  The reference
+   bounds its NCCL waits the same way (safe_stream_wait deadline,
+   src/cuda/nccl/nccl_error.cpp:13-83). */
+nq_status_t nq_set_peer_wait_limit(uint64_t ns);
+uint64_t nq_peer_wait_limit(void);
 
 /* ---- FP8 element-wise, reference codec ------------------------------------
  * Replace src/cuda/quantize/fp8_kernels.cu:29-40 / include/cuda/quantize/
@@ -248,7 +256,7 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  *              stores to every peer;
  *          each reducer warp then counts itself on every rank's completion
  *          counter (nq_allreduce_done_per_job);
- *  finish  with done_target > 0 the kernel returns only once this rank's
+ *  finish  with `done` set the kernel returns only once this rank's
  *          completion counter reaches done_target (its output buffer holds
  *          every reduced tile).
  *
@@ -260,16 +268,18 @@ nq_status_t nq_gemm_simt(const nq_gemm_desc_t* desc, const void* a, const void* 
  *
  * All buffers are symmetric allocations (same size on every rank, mapped into
  * every peer); job pointers address the job's first row.  Counters only
- * grow: zero before epoch 1; the n-th use of a counter set passes epoch n and
- * a job waits for its tiles' counters to reach epoch * tp.  Every rank
- * makes the same sequence of calls.  Waits on other GPUs give up after 5 s
- * and set the device error word (nq_device_error_flags).  A signalling GEMM
+ * grow: zero before the first use; the n-th use of a counter set passes
+ * epoch = n modulo 2^32 and a job waits for its tiles' counters to reach
+ * epoch * tp.  Counters and targets are compared modulo 2^32 (the signed
+ * difference), so they may wrap.  Every rank makes the same sequence of
+ * calls.  Waits on other GPUs give up after nq_peer_wait_limit() ns (5 s by
+ * default) and set the device error word (nq_device_error_flags).  A signalling GEMM
  * needs out_dtype NQ_BF16, epilogue NQ_EPI_NONE, n % 256 == 0; jobs need
  * n % 256 == 0; 1 <= tp <= NQ_MAX_TP. */
 #define NQ_MAX_TP 8
 typedef struct {
     int tp, rank;
-    uint32_t epoch;                      /* 1 for the first use of the counters, then 2, ... */
+    uint32_t epoch;                      /* 1 for the first use of the counters, then 2, ... (mod 2^32) */
     /* signal */
     int signal;                          /* 1: the GEMM's output is a partial */
     uint32_t* signal_flags[NQ_MAX_TP];   /* every rank's counters of the output's tiles */
@@ -282,9 +292,9 @@ typedef struct {
     void* peer_partial[NQ_MAX_TP];       /* peer path: every rank's partial buffer */
     void* peer_out[NQ_MAX_TP];           /* peer path: every rank's output buffer */
     uint32_t* peer_done[NQ_MAX_TP];      /* peer path: every rank's completion counter */
-    /* finish */
-    uint32_t* done;                      /* this rank's completion counter */
-    uint32_t done_target;                /* > 0: wait until *done >= done_target */
+    /* finish (done non-NULL) */
+    uint32_t* done;                      /* this rank's completion counter, or NULL: no finish */
+    uint32_t done_target;                /* wait until *done reaches it (modulo 2^32) */
 } nq_allreduce_desc_t;
 
 /* Tiles (counters) of an m x n output. */

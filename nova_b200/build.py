@@ -23,7 +23,15 @@ SOURCES = ["runtime.cu", "elementwise.cu", "reduce.cu", "gemm.cu"]
 HEADERS = ["nq_internal.h", "ptx.cuh", "codec.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"] + ARCH
-REFERENCE = os.environ.get("NOVA_REFERENCE_DIR", "/root/reference")
+
+
+def reference_dir():
+    """The pplmx/nova source tree used only to build the test-side pins under
+    oracle/_ref/: $NOVA_REFERENCE_DIR, else a checkout named `reference` beside
+    this repository; None when neither exists (the pins are then skipped and
+    any prebuilt oracle/_ref/ files are used as they are)."""
+    cand = os.environ.get("NOVA_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
+    return cand if os.path.isdir(os.path.join(cand, "include", "cuda", "quantize")) else None
 
 
 def _nvcc() -> str:
@@ -74,8 +82,9 @@ def build_oracle() -> None:
     """CPU oracle (test infrastructure) and, where the pplmx/nova sources are
     present, the reference's own code under oracle/_ref/ (checker only)."""
     _run(["make", "-s", "-C", os.path.join(ROOT, "oracle")])
-    if os.path.isdir(os.path.join(REFERENCE, "include", "cuda", "quantize")):
-        _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", f"REF={REFERENCE}"])
+    ref = reference_dir()
+    if ref:
+        _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", f"REF={ref}"])
 
 
 def build_cpp_tests() -> None:

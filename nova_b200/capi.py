@@ -81,6 +81,7 @@ _SIGS = {
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_fp8e5m2_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
     "nq_device_error_flags": [_u32p, _i],
+    "nq_set_peer_wait_limit": [C.c_uint64],
     "nq_mixed_precision_matmul": [_p, _p, _p, _p, _i, _i, _i, _p],
     "nq_fp8_gemm_backward": [_p, _i, _p, _p, _p, _p, _i, _i, _i, _f, _f, _f, _p],
 }
@@ -95,6 +96,9 @@ lib.nq_fp8_gemm_workspace_size.argtypes = [_i, _i, _i]
 lib.nq_gemm_allreduce_counters.restype = C.c_int
 lib.nq_gemm_allreduce_counters.argtypes = [_i, _i]
 gemm_allreduce_counters = lib.nq_gemm_allreduce_counters
+lib.nq_peer_wait_limit.restype = C.c_uint64
+lib.nq_peer_wait_limit.argtypes = []
+peer_wait_limit = lib.nq_peer_wait_limit
 lib.nq_allreduce_done_per_job.restype = C.c_int
 lib.nq_allreduce_done_per_job.argtypes = [_i, _i, _i]
 allreduce_done_per_job = lib.nq_allreduce_done_per_job
@@ -123,7 +127,7 @@ for _n, _a in _SIGS.items():
 
 def exported_symbols():
     return sorted(list(_SIGS) + ["nq_status_string", "nq_last_error", "nq_version", "nq_fp8_gemm_workspace_size",
-                                 "nq_gemm_allreduce_counters", "nq_allreduce_done_per_job"])
+                                 "nq_gemm_allreduce_counters", "nq_allreduce_done_per_job", "nq_peer_wait_limit"])
 
 
 EPI_NONE, EPI_SWIGLU = 0, 1

@@ -22,6 +22,7 @@
 // INT8), for shapes the TMA path cannot take (K or N not a multiple of 16,
 // unaligned pointers) and tiny problems.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -68,11 +69,10 @@ struct ArParams {
     const uint8_t* peer_partial[NQ_MAX_TP];
     uint8_t* peer_out[NQ_MAX_TP];
     uint32_t* peer_done[NQ_MAX_TP];
-    uint32_t* done;
-    uint32_t done_target;
+    uint32_t* done;         // finish: non-NULL
+    uint32_t done_target;   // finish: wait until *done reaches it (modulo 2^32)
+    uint64_t peer_wait_ns;  // bound of a wait on another GPU's counts
 };
-// Upper bound of a wait on another GPU (its kernel may start a little later).
-constexpr uint64_t kPeerWaitLimitNs = 5000000000ull;
 
 // Per-chunk column operands of the epilogue: lane j holds column (col0 + j)'s
 // scale and bias, or the exact identities 1.0 and -0.0 when absent
@@ -400,10 +400,17 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t wan
     }
 }
 
-// Spins (bounded by `limit` ns) until the system-scope value at p >= want.
+// Spins (bounded by `limit` ns) until the system-scope counter at p has
+// reached `want`.  The all-reduce counters only grow and are compared modulo
+// 2^32 (the signed difference), so a counter and a target that both wrapped
+// past 2^32 still compare right; a counter is never more than a forward's
+// worth of counts (far below 2^31) away from its target.
+__device__ __forceinline__ bool counter_reached(uint32_t v, uint32_t want) {
+    return static_cast<int32_t>(v - want) >= 0;
+}
 __device__ __forceinline__ bool wait_sys_geq(const uint32_t* p, uint32_t want, uint32_t* err, uint64_t limit) {
     const uint64_t t0 = globaltimer();
-    while (ld_acquire_sys(p) < want) {
+    while (!counter_reached(ld_acquire_sys(p), want)) {
         if (globaltimer() - t0 > limit) {
             if (err) atomicOr(err, kErrWaitTimeout);
             return false;
@@ -447,7 +454,7 @@ __device__ __forceinline__ void ar_job(const ArParams& ar, int j, int nwarps, in
         for (int i = group;; i += ngroups) {
             const int t = ar.rank + ar.tp * i;
             if (t >= num_tiles) break;
-            if (lane == 0) ok = wait_sys_geq(ar.flags + t, want, err, kPeerWaitLimitNs);
+            if (lane == 0) ok = wait_sys_geq(ar.flags + t, want, err, ar.peer_wait_ns);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             int mb, nb;
@@ -513,8 +520,8 @@ __device__ __forceinline__ void ar_job(const ArParams& ar, int j, int nwarps, in
             }
         }
     }
-    if (ar.done_target && group == 0 && j == 0 && lane == 0 && ok)
-        wait_sys_geq(ar.done, ar.done_target, err, kPeerWaitLimitNs);
+    if (ar.done && group == 0 && j == 0 && lane == 0 && ok)
+        wait_sys_geq(ar.done, ar.done_target, err, ar.peer_wait_ns);
 }
 
 // Job and / or finish without a GEMM: one CTA of AR_WARPS warps per group.
@@ -1220,18 +1227,23 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 nq_status_t get_encode_fn(EncodeTiledFn* fn) {
-    static EncodeTiledFn cached = nullptr;
+    static std::atomic<EncodeTiledFn> cached{nullptr};
     static std::mutex mu;
-    std::lock_guard<std::mutex> lk(mu);
-    if (!cached) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
-            return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled entry point not found");
-        cached = reinterpret_cast<EncodeTiledFn>(p);
+    EncodeTiledFn f = cached.load(std::memory_order_acquire);
+    if (!f) {
+        std::lock_guard<std::mutex> lk(mu);
+        f = cached.load(std::memory_order_relaxed);
+        if (!f) {
+            void* p = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+                return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+            f = reinterpret_cast<EncodeTiledFn>(p);
+            cached.store(f, std::memory_order_release);
+        }
     }
-    *fn = cached;
+    *fn = f;
     return NQ_SUCCESS;
 }
 
@@ -1255,16 +1267,13 @@ nq_status_t make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 
 // The shared-memory opt-in is a per-device function attribute.
 template <class F>
-nq_status_t ensure_smem_attr(F kern, int bytes, int device, uint64_t* flags) {
+nq_status_t ensure_smem_attr(F kern, int bytes, int device, std::atomic<uint64_t>* flags) {
     static std::mutex mu;
-    std::lock_guard<std::mutex> lk(mu);
-    const uint64_t bit = 1ull << (device & 63);
-    if (!(*flags & bit)) {
+    return once_per_device(*flags, mu, device, [&]() -> nq_status_t {
         NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                       "cudaFuncSetAttribute(gemm)");
-        *flags |= bit;
-    }
-    return NQ_SUCCESS;
+        return NQ_SUCCESS;
+    });
 }
 
 uint32_t gemm_idesc(const nq_gemm_desc_t& d, bool i8, bool kn, uint32_t m, uint32_t n) {
@@ -1313,13 +1322,13 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
     auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU, AR>;
-    static uint64_t attr_set = 0;
+    static std::atomic<uint64_t> attr_set{0};
     st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
     // as many clusters as can be resident at once (an SM without a free partner
     // in its GPC cannot host half of a pair)
-    static int max_clusters[64] = {};
-    if (!max_clusters[di.device & 63]) {
+    static std::atomic<int> max_clusters[64];
+    if (!max_clusters[di.device & 63].load(std::memory_order_relaxed)) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (di.sm_count / 2));
         cfg.blockDim = dim3(AR ? P_THREADS_AR : P_THREADS);
@@ -1329,10 +1338,10 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
             cudaGetLastError();
             nc = di.sm_count / 2;
         }
-        max_clusters[di.device & 63] = nc;
+        max_clusters[di.device & 63].store(nc, std::memory_order_relaxed);
     }
     const int tiles = ((d.m + P_BM - 1) / P_BM) * ((d.n + P_BN - 1) / P_BN);
-    const int clusters = std::max(1, std::min(tiles, max_clusters[di.device & 63]));
+    const int clusters = std::max(1, std::min(tiles, max_clusters[di.device & 63].load(std::memory_order_relaxed)));
     constexpr int threads = AR ? P_THREADS_AR : P_THREADS;
     const int grid = 2 * clusters;
     const int kblocks = (d.k + BK - 1) / BK;
@@ -1381,7 +1390,7 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
                               : make_idesc(1u, d.b_format == NQ_E5M2 ? 1u : 0u, d.a_format == NQ_E5M2 ? 1u : 0u, 0u,
                                            128u, BT, KN ? 1u : 0u);
     auto kern = k_gemm_decode<I8, KN, BT>;
-    static uint64_t attr_set = 0;
+    static std::atomic<uint64_t> attr_set{0};
     st = ensure_smem_attr(kern, Cfg::SMEM, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
     const long long total = static_cast<long long>((d.n + 127) / 128) * ((d.k + BK - 1) / BK);
@@ -1442,7 +1451,7 @@ nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, con
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, BM, BN);
     auto kern = k_gemm_tc<I8, KN>;
-    static uint64_t attr_set = 0;
+    static std::atomic<uint64_t> attr_set{0};
     st = ensure_smem_attr(kern, SMEM_BYTES, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
     const int tiles = ((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
@@ -1536,8 +1545,9 @@ namespace {
 nq_status_t fill_ar(const nq_allreduce_desc_t* r, ArParams* ar) {
     std::memset(ar, 0, sizeof(*ar));
     if (!r) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: null descriptor");
-    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp || r->epoch == 0)
-        return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: tp / rank / epoch");
+    if (r->tp < 1 || r->tp > NQ_MAX_TP || r->rank < 0 || r->rank >= r->tp)
+        return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: tp / rank");
+    ar->peer_wait_ns = peer_wait_limit_ns();
     ar->tp = r->tp;
     ar->rank = r->rank;
     ar->epoch = r->epoch;
@@ -1573,8 +1583,7 @@ nq_status_t fill_ar(const nq_allreduce_desc_t* r, ArParams* ar) {
             ar->peer_done[p] = r->peer_done[p];
         }
     }
-    if (r->done_target) {
-        if (!r->done) return fail(NQ_ERROR_INVALID_VALUE, "all-reduce: done counter");
+    if (r->done) {
         ar->done = r->done;
         ar->done_target = r->done_target;
     }
@@ -1624,7 +1633,7 @@ nq_status_t allreduce_finish_impl(const nq_allreduce_desc_t* r, cudaStream_t s) 
     nq_status_t st = fill_ar(r, &ar);
     if (st != NQ_SUCCESS) return st;
     if (ar.signal) return fail(NQ_ERROR_INVALID_VALUE, "nq_allreduce_finish: nothing to signal without a GEMM");
-    if (ar.m == 0 && ar.done_target == 0) return NQ_SUCCESS;
+    if (ar.m == 0 && !ar.done) return NQ_SUCCESS;
     DeviceInfo di;
     st = current_device(&di);
     if (st != NQ_SUCCESS) return st;

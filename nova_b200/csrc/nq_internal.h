@@ -3,8 +3,10 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "../../include/nova_q.h"
@@ -35,7 +37,25 @@ void scratch_free(void* p, cudaStream_t s);
 // error bits into it), or nullptr if it cannot be resolved.
 uint32_t* device_error_word();
 
+// Bound (ns) of a kernel's wait on counts that other GPUs send (the fused
+// all-reduce); nq_set_peer_wait_limit changes it for kernels launched later.
+uint64_t peer_wait_limit_ns();
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Runs init() once per device for one call site (e.g. a kernel's shared-memory
+// opt-in, a per-device function attribute).  Bit `device` of `done` is read
+// without a lock; only a device's first call takes `mu`.
+template <class F>
+nq_status_t once_per_device(std::atomic<uint64_t>& done, std::mutex& mu, int device, F init) {
+    const uint64_t bit = 1ull << (device & 63);
+    if (done.load(std::memory_order_acquire) & bit) return NQ_SUCCESS;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.load(std::memory_order_relaxed) & bit) return NQ_SUCCESS;
+    nq_status_t st = init();
+    if (st == NQ_SUCCESS) done.fetch_or(bit, std::memory_order_release);
+    return st;
+}
 
 }  // namespace nq
 

@@ -481,17 +481,14 @@ nq_status_t launch_quant_rows_bulk(const void* src, nq_dtype_t dt, uint8_t* dst,
     const int smem = static_cast<int>(stages * rb + 8 * stages);
     auto launch = [&](auto kern, const auto* typed_src) -> nq_status_t {
         static std::mutex mu;
-        static uint64_t attr_set = 0;
-        {
-            std::lock_guard<std::mutex> lk(mu);
-            const uint64_t bit = 1ull << (di.device & 63);
-            if (!(attr_set & bit)) {
-                NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(kBulkRowSmem + 64)),
-                              "cudaFuncSetAttribute(quantize_rows)");
-                attr_set |= bit;
-            }
-        }
+        static std::atomic<uint64_t> attr_set{0};
+        nq_status_t st = once_per_device(attr_set, mu, di.device, [&]() -> nq_status_t {
+            NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kBulkRowSmem + 64)),
+                          "cudaFuncSetAttribute(quantize_rows)");
+            return NQ_SUCCESS;
+        });
+        if (st != NQ_SUCCESS) return st;
         int per_sm = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1) {
             cudaGetLastError();
@@ -519,16 +516,13 @@ nq_status_t launch_quant_rows_warp(const void* src, nq_dtype_t dt, uint8_t* dst,
     const int smem = static_cast<int>(warps * stages * rb + warps * stages * 8);
     auto launch = [&](auto kern, const auto* typed_src) -> nq_status_t {
         static std::mutex mu;
-        static uint64_t attr_set = 0;
-        {
-            std::lock_guard<std::mutex> lk(mu);
-            const uint64_t bit = 1ull << (di.device & 63);
-            if (!(attr_set & bit)) {
-                NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
-                              "cudaFuncSetAttribute(quantize_rows)");
-                attr_set |= bit;
-            }
-        }
+        static std::atomic<uint64_t> attr_set{0};
+        nq_status_t st = once_per_device(attr_set, mu, di.device, [&]() -> nq_status_t {
+            NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                          "cudaFuncSetAttribute(quantize_rows)");
+            return NQ_SUCCESS;
+        });
+        if (st != NQ_SUCCESS) return st;
         int per_sm = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1) {
             cudaGetLastError();
@@ -836,21 +830,27 @@ namespace {
 
 // Host code may not pass the symbol itself to a kernel (on the host it names
 // a stand-in, not device memory): its device address is looked up once per
-// device, with that device current, and cached.
+// device, with that device current, and cached.  Later calls read the cached
+// address without a lock; only a device's first call takes the mutex.
 nq_status_t noalloc_scratch(uint32_t** out) {
     static std::mutex mu;
-    static uint32_t* addr[64] = {};
+    static std::atomic<uint32_t*> addr[64];
     int dev = -1;
     NQ_CHECK_CUDA(cudaGetDevice(&dev), "nq_quantize_cols_noalloc: cudaGetDevice");
     if (dev < 0 || dev >= 64) return fail(NQ_ERROR_NO_DEVICE, "nq_quantize_cols_noalloc: device ordinal out of range");
-    std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_col_amax);
-        if (e != cudaSuccess) return cuda_status(e, "nq_quantize_cols_noalloc: cudaGetSymbolAddress");
-        addr[dev] = static_cast<uint32_t*>(p);
+    uint32_t* a = addr[dev].load(std::memory_order_acquire);
+    if (!a) {
+        std::lock_guard<std::mutex> lk(mu);
+        a = addr[dev].load(std::memory_order_relaxed);
+        if (!a) {
+            void* p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_col_amax);
+            if (e != cudaSuccess) return cuda_status(e, "nq_quantize_cols_noalloc: cudaGetSymbolAddress");
+            a = static_cast<uint32_t*>(p);
+            addr[dev].store(a, std::memory_order_release);
+        }
     }
-    *out = addr[dev];
+    *out = a;
     return NQ_SUCCESS;
 }
 }  // namespace

@@ -1,5 +1,6 @@
 // Runtime support of libnova_q: status strings, thread-local error text,
 // device properties, the scratch pool and the device-side error word.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -12,12 +13,21 @@ __device__ uint32_t nq_device_error_word = 0;
 
 namespace nq {
 
+// Per-device caches are filled once under g_mu and then read without a lock
+// (an acquire load of the slot), so no launch path takes a lock after a
+// device's first call.
 namespace {
 thread_local std::string g_last_error;
 std::mutex g_mu;
 DeviceInfo g_info[64];
-cudaMemPool_t g_pool[64] = {};
+std::atomic<bool> g_info_ready[64];
+std::atomic<cudaMemPool_t> g_pool[64];
+std::atomic<uint32_t*> g_err_word[64];
+constexpr uint64_t kDefaultPeerWaitNs = 5000000000ull;  // 5 s: a peer's kernel may start a little later
+std::atomic<uint64_t> g_peer_wait_ns{kDefaultPeerWaitNs};
 }  // namespace
+
+uint64_t peer_wait_limit_ns() { return g_peer_wait_ns.load(std::memory_order_relaxed); }
 
 nq_status_t fail(nq_status_t st, const std::string& msg) {
     g_last_error = msg;
@@ -37,18 +47,22 @@ nq_status_t current_device(DeviceInfo* out) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
     if (dev < 0 || dev >= 64) return fail(NQ_ERROR_NO_DEVICE, "device ordinal out of range");
-    std::lock_guard<std::mutex> lk(g_mu);
-    DeviceInfo& d = g_info[dev];
-    if (d.device != dev) {
-        cudaDeviceProp p;
-        e = cudaGetDeviceProperties(&p, dev);
-        if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
-        d.device = dev;
-        d.sm_count = p.multiProcessorCount;
-        d.major = p.major;
-        d.minor = p.minor;
-        d.max_smem_optin = p.sharedMemPerBlockOptin;
+    if (!g_info_ready[dev].load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_info_ready[dev].load(std::memory_order_relaxed)) {
+            cudaDeviceProp p;
+            e = cudaGetDeviceProperties(&p, dev);
+            if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
+            DeviceInfo& w = g_info[dev];
+            w.device = dev;
+            w.sm_count = p.multiProcessorCount;
+            w.major = p.major;
+            w.minor = p.minor;
+            w.max_smem_optin = p.sharedMemPerBlockOptin;
+            g_info_ready[dev].store(true, std::memory_order_release);
+        }
     }
+    const DeviceInfo& d = g_info[dev];
     if (d.major != 10)
         return fail(NQ_ERROR_NO_DEVICE, "libnova_q is built for sm_100a (B200); the current device is sm_" +
                                             std::to_string(d.major) + std::to_string(d.minor));
@@ -59,20 +73,22 @@ nq_status_t current_device(DeviceInfo* out) {
 nq_status_t scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
     int dev = -1;
     NQ_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-    cudaMemPool_t pool;
-    {
+    if (dev < 0 || dev >= 64) return fail(NQ_ERROR_NO_DEVICE, "device ordinal out of range");
+    cudaMemPool_t pool = g_pool[dev].load(std::memory_order_acquire);
+    if (!pool) {
         std::lock_guard<std::mutex> lk(g_mu);
-        if (!g_pool[dev]) {
+        pool = g_pool[dev].load(std::memory_order_relaxed);
+        if (!pool) {
             cudaMemPoolProps props = {};
             props.allocType = cudaMemAllocationTypePinned;
             props.location.type = cudaMemLocationTypeDevice;
             props.location.id = dev;
-            NQ_CHECK_CUDA(cudaMemPoolCreate(&g_pool[dev], &props), "cudaMemPoolCreate");
+            NQ_CHECK_CUDA(cudaMemPoolCreate(&pool, &props), "cudaMemPoolCreate");
             uint64_t keep = UINT64_MAX;  // keep freed blocks cached in the pool
-            NQ_CHECK_CUDA(cudaMemPoolSetAttribute(g_pool[dev], cudaMemPoolAttrReleaseThreshold, &keep),
+            NQ_CHECK_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep),
                           "cudaMemPoolSetAttribute");
+            g_pool[dev].store(pool, std::memory_order_release);
         }
-        pool = g_pool[dev];
     }
     NQ_CHECK_CUDA(cudaMallocFromPoolAsync(p, bytes, pool, s), "cudaMallocFromPoolAsync");
     return NQ_SUCCESS;
@@ -85,16 +101,19 @@ void scratch_free(void* p, cudaStream_t s) {
 uint32_t* device_error_word() {
     // Host code cannot name a __device__ variable's address directly: the
     // symbol's address is looked up once per device with that device current.
-    static uint32_t* addr[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    uint32_t* a = g_err_word[dev].load(std::memory_order_acquire);
+    if (a) return a;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!addr[dev]) {
+    a = g_err_word[dev].load(std::memory_order_relaxed);
+    if (!a) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, nq_device_error_word) != cudaSuccess) return nullptr;
-        addr[dev] = static_cast<uint32_t*>(p);
+        a = static_cast<uint32_t*>(p);
+        g_err_word[dev].store(a, std::memory_order_release);
     }
-    return addr[dev];
+    return a;
 }
 
 }  // namespace nq
@@ -117,6 +136,13 @@ const char* nq_status_string(nq_status_t s) {
 const char* nq_last_error(void) { return nq::g_last_error.c_str(); }
 
 int nq_version(void) { return 100; }
+
+nq_status_t nq_set_peer_wait_limit(uint64_t ns) {
+    nq::g_peer_wait_ns.store(ns ? ns : nq::kDefaultPeerWaitNs, std::memory_order_relaxed);
+    return NQ_SUCCESS;
+}
+
+uint64_t nq_peer_wait_limit(void) { return nq::peer_wait_limit_ns(); }
 
 nq_status_t nq_device_error_flags(uint32_t* flags, int clear) {
     if (!flags) return nq::fail(NQ_ERROR_INVALID_VALUE, "nq_device_error_flags: flags is null");

@@ -201,7 +201,9 @@ class SymmetricAllReduce:
         `job` = chunk to reduce, `finish` = wait for every chunk of this epoch."""
         nq = self.nq
         d = nq.AllreduceDesc()
-        d.tp, d.rank, d.epoch = self.tp, self.rank, st.epoch
+        # epochs and counter targets are taken modulo 2^32 (the kernels compare
+        # counters by their signed difference, so wrapping is harmless)
+        d.tp, d.rank, d.epoch = self.tp, self.rank, st.epoch & 0xFFFFFFFF
         if signal is not None:
             d.signal = 1
             for r in range(self.tp):
@@ -217,7 +219,7 @@ class SymmetricAllReduce:
                 d.peer_partial[r], d.peer_out[r], d.peer_done[r] = st.pp[r] + row, st.po[r] + row, st.pd[r]
         if finish:
             d.done = st.done.data_ptr()
-            d.done_target = st.epoch * st.per_forward
+            d.done_target = (st.epoch * st.per_forward) & 0xFFFFFFFF
         return d
 
     def multicast(self):

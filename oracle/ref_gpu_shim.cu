@@ -61,6 +61,17 @@ int ref_gpu_fp8_gemm(const uint8_t* a, const uint8_t* b, float* c, int m, int k,
     return (int)cudaDeviceSynchronize();
 }
 
+// MSECalibrator::calibrate of the reference (calibrator.cpp:158-190) on a
+// HOST pointer: its scale search reads data[i] on the host, so only host
+// memory is valid there.
+int ref_gpu_mse_calibrate(const float* host_data, size_t n, int sym, float* out5) {
+    MSECalibrator c(sym != 0);
+    CalibrationResult r = c.calibrate(host_data, n, 0);
+    out5[0] = r.scale; out5[1] = r.zero_point; out5[2] = r.symmetric ? 1.0f : 0.0f;
+    out5[3] = r.min_val; out5[4] = r.max_val;
+    return (int)cudaDeviceSynchronize();
+}
+
 int ref_gpu_minmax_calibrate(const float* data, size_t n, int sym, float* out5) {
     MinMaxCalibrator c(sym != 0);
     CalibrationResult r = c.calibrate(data, n, 0);

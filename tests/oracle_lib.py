@@ -233,6 +233,7 @@ def ref_gpu():
         ("ref_gpu_build_histogram", [_p, _p, _sz, _f, _f, _i]),
         ("ref_gpu_fp8_gemm", [_p, _p, _p, _i, _i, _i, _f, _f, _f]),
         ("ref_gpu_minmax_calibrate", [_p, _sz, _i, _p]),
+        ("ref_gpu_mse_calibrate", [_p, _sz, _i, _p]),
     ]:
         fn = getattr(r, name)
         fn.restype = _i

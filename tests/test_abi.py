@@ -64,9 +64,7 @@ def test_gemm_allreduce_argument_checks_without_gpu():
     ar.tp, ar.rank, ar.epoch = 2, 0, 1
     run = lambda: capi.gemm_allreduce.raw(C.byref(d), C.byref(ar), 16, 16, 16, None)
     assert capi.gemm_allreduce.raw(None, C.byref(ar), 16, 16, 16, None) == 1     # null descriptor
-    ar.epoch = 0
-    assert run() == 1                                                              # epoch 0
-    ar.epoch, ar.tp = 1, 9
+    ar.tp = 9
     assert run() == 1                                                              # tp > NQ_MAX_TP
     ar.tp, ar.signal = 2, 1
     assert run() == 1                                                              # signal without counters
@@ -82,7 +80,9 @@ def test_gemm_allreduce_argument_checks_without_gpu():
     assert run() == 1                                                              # job without peer pointers
     assert capi.allreduce_finish.raw(C.byref(ar), None) == 1                       # finish cannot signal
     ar.signal, ar.m, ar.done_target = 0, 0, 5
-    assert capi.allreduce_finish.raw(C.byref(ar), None) == 1                       # finish without a counter
+    assert capi.allreduce_finish.raw(C.byref(ar), None) == 0                       # no job, no `done`: nothing to do
+    ar.rank = 2
+    assert capi.allreduce_finish.raw(C.byref(ar), None) == 1                       # rank >= tp
 
 
 def test_fp8_backward_argument_checks_without_gpu():

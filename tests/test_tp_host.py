@@ -168,6 +168,41 @@ def test_fused_allreduce_descriptors():
     assert d.mc_partial is None and d.peer_out[3] == (43 << 20)
     last = nq.gemm_allreduce_counters(bounds[-1][1] - bounds[-1][0], n)
     assert per_forward == 5 * (tiles - last) + 4 * last
+    # counters wrap: near 2^32 forwards the epoch and the completion target are
+    # the use count and its counter total modulo 2^32, and the finish is keyed
+    # on `done`, so a target that wraps to exactly 0 still waits
+    for epoch in ((1 << 32) - 2, (1 << 32) - 1, 1 << 32, (1 << 32) + 1):
+        st.epoch = epoch - 1
+        ar.begin(st)
+        d = ar.desc(st, signal=2, job=2, finish=True)
+        assert d.epoch == epoch % (1 << 32)
+        assert d.done_target == (epoch * per_forward) % (1 << 32) and d.done == 2 << 20
+    st.per_forward, st.epoch = 1 << 31, 2
+    d = ar.desc(st, finish=True)
+    assert d.done_target == 0 and d.done == 2 << 20
+
+
+def _counter_reached(v, want):
+    """The kernels' counter compare (gemm.cu counter_reached): v has reached
+    want when their difference modulo 2^32, read as a signed 32-bit value, is
+    not negative."""
+    diff = (v - want) % (1 << 32)
+    return diff < (1 << 31)
+
+
+def test_counter_compare_wraps():
+    """A counter that wrapped past 2^32 still compares right against a target
+    that wrapped too, and one a forward short of it still waits."""
+    per_forward, tp_ = 5 * 2048, 8
+    for epoch in (1, 2, (1 << 32) // per_forward, (1 << 32) // per_forward + 1, (1 << 32) - 1):
+        target = (epoch * per_forward) % (1 << 32)
+        assert _counter_reached(target, target)
+        assert not _counter_reached((target - 1) % (1 << 32), target)
+        assert not _counter_reached((target - per_forward) % (1 << 32), target)
+        assert _counter_reached((target + per_forward) % (1 << 32), target)   # a peer already one forward on
+        flag_want = (epoch * tp_) % (1 << 32)
+        assert _counter_reached(flag_want, flag_want)
+        assert not _counter_reached((flag_want - 1) % (1 << 32), flag_want)
 
 
 def test_layer_argument_checks_without_gpu():

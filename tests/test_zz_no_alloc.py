@@ -20,10 +20,10 @@ def nq(cuda):
     return capi
 
 
-def run(nq, fn, x, fmt):
+def run(nq, fn, x, fmt, offset=0):
     from gpu_util import dev, empty, host, ptr, stream
     rows, cols = x.shape
-    d_x, d_q, d_s = dev(x), empty(rows * cols), empty(4 * cols)
+    d_x, d_q, d_s = dev(x, offset), empty(rows * cols), empty(4 * cols)
     fn(ptr(d_x), ptr(d_q), ptr(d_s), rows, cols, fmt, stream())
     return host(d_q, np.uint8, (rows, cols)), host(d_s, np.float32)
 
@@ -38,6 +38,20 @@ def test_noalloc_matches_pooled_entry_point_twice(nq, fmt):
         q_ref, s_ref = run(nq, nq.quantize_cols, x, fmt)
         np.testing.assert_array_equal(s_new, s_ref)
         np.testing.assert_array_equal(q_new, q_ref)
+
+
+@pytest.mark.parametrize("rows,cols,offset", [(37, 1027, 0), (19, 1027, 4), (3, 65536, 0)])
+def test_noalloc_ragged_widths_and_the_limit(nq, rows, cols, offset):
+    """Widths that are not a multiple of 4 (the kernels' scalar column tail),
+    an unaligned source, and the largest width the fixed scratch holds."""
+    rng = np.random.default_rng(rows * cols)
+    for scale in (1.0, 0.01):   # two calls in a row, the second with smaller maxima
+        x = (rng.standard_normal((rows, cols)) * scale).astype(np.float32)
+        for fmt in (0, 2):
+            q_new, s_new = run(nq, nq.quantize_cols_noalloc, x, fmt, offset)
+            q_ref, s_ref = run(nq, nq.quantize_cols, x, fmt, offset)
+            np.testing.assert_array_equal(s_new, s_ref)
+            np.testing.assert_array_equal(q_new, q_ref)
 
 
 def test_noalloc_rejects_widths_beyond_its_scratch(nq):
