@@ -229,6 +229,21 @@ typedef struct {
 
 nq_status_t nq_gemm(const nq_gemm_desc_t* desc, const void* a, const void* b, void* out,
                     nq_stream_t s);
+/* W8A8 GEMM with the per-token dynamic quantization of the activations fused
+   into the kernel (a row-parallel or up-projection layer fed bf16
+   activations).  x: m x k bf16, row-major.  The kernel quantizes every row of
+   x exactly as nq_quantize_rows(x, NQ_BF16, a_codes, a_scales, m, k, NQ_E4M3)
+   does -- bit-identical codes and scales, written to a_codes (m x k) and
+   a_scales (m) -- and multiplies the codes by B with a_scales as the
+   epilogue's row scale, in ONE launch: the grid's warps quantize the rows
+   first and publish each 128-row block, and a tile's A loads wait (bounded)
+   for its block.  desc: a_format NQ_E4M3, b_format E4M3 or E5M2, row_scale
+   NULL, out_dtype NQ_BF16 or NQ_F32, epilogue NONE or SWIGLU; k, n multiples
+   of 16 and 16-byte aligned pointers.  No reference counterpart: the
+   reference's FP8GEMM::forward (fp8_gemm.cu:164-188) takes codes already
+   quantized per tensor. */
+nq_status_t nq_gemm_quant_a(const nq_gemm_desc_t* desc, const void* x, uint8_t* a_codes, float* a_scales,
+                            const void* b, void* out, nq_stream_t s);
 /* The same GEMM on the CUDA cores only (one thread per output, sequential-k
    fp32 FMA or int32 accumulation): an exactly ordered variant for checking
    and for shapes far below one tensor-core tile. */

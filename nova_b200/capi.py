@@ -76,6 +76,7 @@ _SIGS = {
     "nq_quantize_cols_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "nq_gemm": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_gemm_simt": [C.POINTER(GemmDesc), _p, _p, _p, _p],
+    "nq_gemm_quant_a": [C.POINTER(GemmDesc), _p, _p, _p, _p, _p, _p],
     "nq_gemm_allreduce": [C.POINTER(GemmDesc), C.POINTER(AllreduceDesc), _p, _p, _p, _p],
     "nq_allreduce_finish": [C.POINTER(AllreduceDesc), _p],
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],

@@ -17,6 +17,7 @@
 //   (int8_kernels.cu:30-35).
 #pragma once
 
+#include <cfloat>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -137,6 +138,47 @@ __device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
+}
+
+// Per-row / per-column scaling: scale = amax / qmax (1 for an all-zero row)
+// and q = encode(x * inv) with inv = qmax / amax, one IEEE division per row.
+// When qmax / amax overflows (amax < qmax / FLT_MAX) the row is divided by
+// its scale instead, so a row of tiny values never meets an infinite
+// multiplier.  The choice is uniform over a row, so it costs no divergence.
+struct RowScale {
+    float s, inv;
+    bool mul;
+};
+template <int F>
+__device__ __forceinline__ RowScale row_scale(float a) {
+    constexpr float q = FmtTraits<F>::qmax;
+    if (!(a > 0.0f)) return RowScale{1.0f, 1.0f, true};
+    const float inv = q / a;
+    return RowScale{a / q, inv, inv <= FLT_MAX};
+}
+template <bool MUL>
+__device__ __forceinline__ float scale_apply(float x, const RowScale& r) {
+    return MUL ? x * r.inv : x / r.s;
+}
+
+// Element e of a 16-byte vector of fp32 (4) or bf16 (8) values.
+template <class In>
+__device__ __forceinline__ float vec_elem(const uint4& q, int e) {
+    constexpr int EPV = 16 / sizeof(In);
+    const uint32_t w = e < EPV / 4 ? q.x : (e < EPV / 2 ? q.y : (e < 3 * EPV / 4 ? q.z : q.w));
+    if (sizeof(In) == 2) return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
+    return __uint_as_float(w);
+}
+template <int F, class In, bool MUL>
+__device__ __forceinline__ void encode_vec(const uint4& q, uint8_t* out, const RowScale& r) {
+    constexpr int EPV = 16 / sizeof(In);
+    uint32_t codes[EPV / 2];
+#pragma unroll
+    for (int e = 0; e < EPV; e += 2)
+        codes[e / 2] = ocp_encode2<F>(scale_apply<MUL>(vec_elem<In>(q, e), r),
+                                           scale_apply<MUL>(vec_elem<In>(q, e + 1), r));
+    if (EPV == 8) *reinterpret_cast<uint2*>(out) = make_uint2(codes[0] | (codes[1] << 16), codes[2] | (codes[3] << 16));
+    else *reinterpret_cast<uint32_t*>(out) = codes[0] | (codes[1] << 16);
 }
 
 }  // namespace dev

@@ -351,21 +351,89 @@ constexpr int P_THREADS = 320;
 constexpr int P_EPI_WARPS = 8;
 constexpr int P_A_STAGE = 128 * BK;  // 16 KB per CTA
 constexpr int P_B_STAGE = 128 * BK;  // 16 KB per CTA
-// Tail split: when the last wave is at most half full, its tiles are cut along
-// K into two parts that run side by side on otherwise idle CTA pairs.  Part 1
-// parks its raw accumulators in `ws` and counts its 8 epilogue warps in
-// `flags`; part 0 waits for them, adds the partial (exact for int32) and
-// writes the tile.
-struct SplitTail {
-    int full_units;   // units [0, full_units) are whole tiles
-    int rem;          // tiles in the tail wave
-    int split;        // K parts per tail tile: 1 (no split) or 2
-    uint32_t* ws;     // [rem][256 x 256] accumulators of part 1
-    uint32_t* flags;  // [rem] arrivals of part 1's 8 epilogue warps
+// Stream-K schedule.  Tiles [0, dp_tiles) are whole tiles dealt round-robin
+// to the clusters; the k-blocks of the last sk_tiles tiles are cut into one
+// equal contiguous range per cluster, so the last (1 + fraction) waves keep
+// every cluster busy instead of leaving part of the machine idle.  A tile cut
+// by range boundaries is finished by the cluster holding its first k-block,
+// which reaches that part last (it ends that cluster's range); every later
+// cluster touching the tile does its part first, parks the raw accumulators
+// in its own workspace slot and counts its 16 epilogue warps in its flag.  The
+// finishing cluster adds the parked parts in cluster order before its
+// epilogue: deterministic, exact for int32.  A cluster parks at most once
+// (only its first stream-K item can start inside a tile).
+struct StreamK {
+    int dp_tiles;     // whole tiles, round-robin
+    int sk_tiles;     // tiles whose k-blocks are shared out (0: none)
+    uint32_t* ws;     // [clusters][256 x 256] parked accumulators
+    uint32_t* flags;  // [clusters] epilogue warps that parked
 };
 struct Unit {
-    int tile, part, kb0, kb1;
+    int tile, kb0, kb1;
+    int park;            // the accumulators go to this cluster's workspace slot
+    int c_first, c_last; // the tile's later parts, parked by these clusters (none if c_first > c_last)
 };
+__host__ __device__ __forceinline__ long long sk_begin(long long total, int c, int nclusters) {
+    return total * c / nclusters;
+}
+// Work items of `cluster`: its whole tiles, then one item per tile its
+// stream-K range touches.
+__device__ __forceinline__ int sched_whole(const StreamK& sk, int cluster, int nclusters) {
+    return sk.dp_tiles > cluster ? (sk.dp_tiles - cluster + nclusters - 1) / nclusters : 0;
+}
+__device__ __forceinline__ int sched_items(const StreamK& sk, int kblocks, int cluster, int nclusters) {
+    int n = sched_whole(sk, cluster, nclusters);
+    if (sk.sk_tiles > 0) {
+        const long long total = static_cast<long long>(sk.sk_tiles) * kblocks;
+        const long long b0 = sk_begin(total, cluster, nclusters), b1 = sk_begin(total, cluster + 1, nclusters);
+        if (b1 > b0) n += static_cast<int>((b1 - 1) / kblocks - b0 / kblocks + 1);
+    }
+    return n;
+}
+__device__ __forceinline__ Unit sched_unit(const StreamK& sk, int kblocks, int cluster, int nclusters, int n_whole,
+                                           int j) {
+    if (j < n_whole) return Unit{cluster + j * nclusters, 0, kblocks, 0, 1, 0};
+    const long long total = static_cast<long long>(sk.sk_tiles) * kblocks;
+    const long long b0 = sk_begin(total, cluster, nclusters), b1 = sk_begin(total, cluster + 1, nclusters);
+    const long long lt = b0 / kblocks + (j - n_whole);
+    const long long t0 = lt * kblocks, t1 = t0 + kblocks;
+    Unit u;
+    u.tile = sk.dp_tiles + static_cast<int>(lt);
+    u.kb0 = static_cast<int>((b0 > t0 ? b0 : t0) - t0);
+    u.kb1 = static_cast<int>((b1 < t1 ? b1 : t1) - t0);
+    u.park = u.kb0 > 0;
+    u.c_first = cluster + 1;
+    u.c_last = cluster;
+    if (!u.park && b1 < t1) {
+        // the tile runs past this range: the clusters whose ranges start inside it
+        u.c_last = u.c_first;
+        while (u.c_last + 1 < nclusters && sk_begin(total, u.c_last + 1, nclusters) < t1) ++u.c_last;
+    }
+    return u;
+}
+// Parked accumulators of one epilogue warp (w16 = its index among the pair's
+// 16 epilogue warps): 4 chunks x 8 uint4 x 32 lanes, lane-fastest so that each
+// warp-wide access is 512 contiguous bytes.
+__device__ __forceinline__ uint4* park_slot(uint32_t* ws, int cluster, int w16) {
+    return reinterpret_cast<uint4*>(ws + static_cast<size_t>(cluster) * (256 * 256)) + static_cast<size_t>(w16) * (4 * 8 * 32);
+}
+// acc[4q .. 4q+3] += parked values (int32 exact, fp32 one rounding each).
+template <bool INT_ACC>
+__device__ __forceinline__ void add_parked4(uint32_t (&acc)[32], int q, const uint4& v) {
+    const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int e = 4 * q + t;
+        if (INT_ACC) acc[e] = static_cast<uint32_t>(static_cast<int32_t>(acc[e]) + static_cast<int32_t>(p[t]));
+        else acc[e] = __float_as_uint(__fadd_rn(__uint_as_float(acc[e]), __uint_as_float(p[t])));
+    }
+}
+// acc += one parked 32-column chunk.
+template <bool INT_ACC>
+__device__ __forceinline__ void add_parked(uint32_t (&acc)[32], const uint4 (&v)[8]) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) add_parked4<INT_ACC>(acc, q, v[q]);
+}
 // Tile order of the persistent schedule: bands of P_BAND M-tiles; inside a
 // band the tiles walk N, M fastest.  The clusters in flight at any moment
 // then share at most P_BAND A panels and ~clusters/P_BAND B panels, a working
@@ -378,12 +446,6 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
     const int local = tile - band * P_BAND * n_tiles;
     mb = band * P_BAND + local % rows;
     nb = local / rows;
-}
-__device__ __forceinline__ Unit decode_unit(int u, const SplitTail& st, int kblocks) {
-    if (st.split <= 1 || u < st.full_units) return Unit{u, 0, 0, kblocks};
-    const int v = u - st.full_units;
-    const int part = v / st.rem;
-    return Unit{st.full_units + v % st.rem, part, part * kblocks / st.split, (part + 1) * kblocks / st.split};
 }
 // Spins (bounded) until *flag >= want, reading with acquire semantics.
 __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t want, uint32_t* err) {
@@ -427,6 +489,136 @@ constexpr int P_EPI_SLOT = 4096;
 constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_SLOT;
 constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES + 256;
 
+
+// A operand quantized inside the GEMM (per-token dynamic quantization fused
+// into the kernel): bf16 activations x (rows x cols), their E4M3 codes and
+// per-row scales written by phase 1, and the count of rows done.
+struct QuantA {
+    const uint16_t* x;
+    uint8_t* codes;
+    float* scales;
+    uint32_t* done;  // rows quantized so far; zero before the launch
+    int rows, cols;
+};
+constexpr int QA_REG_VECS = 16;  // rows up to 16 * 32 * 8 = 4096 values stay in registers
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+template <bool MUL>
+__device__ __forceinline__ void encode_row_vecs(const uint4* v, int n, int lane, int nv, uint8_t* out,
+                                                const RowScale& rs) {
+#pragma unroll
+    for (int i = 0; i < QA_REG_VECS; ++i) {
+        const int idx = lane + 32 * i;
+        if (i < n && idx < nv) encode_vec<kE4M3, uint16_t, MUL>(v[i], out + idx * 8, rs);
+    }
+}
+// Phase 1: warp w of the grid takes rows w, w + nw, ...: the row's amax, its
+// codes q = E4M3(x * (448 / amax)) and scale amax / 448 -- the arithmetic of
+// nq_quantize_rows, bit for bit.  When its rows are written the warp counts
+// them on qa.done (a release, after a proxy fence: TMA reads the codes back).
+// The GEMM roles then wait once for all rows (qa_wait_all): one acquire and
+// one cross-proxy fence per thread, instead of one per tile, which stalled
+// the TMA producer between tiles.
+__device__ void quant_rows_phase(const QuantA& qa, int warp, int lane, int warps_per_cta) {
+    const int nv = qa.cols / 8;
+    const long long nw = static_cast<long long>(gridDim.x) * warps_per_cta;
+    uint32_t mine = 0;
+    for (long long r = static_cast<long long>(blockIdx.x) * warps_per_cta + warp; r < qa.rows; r += nw, ++mine) {
+        const uint16_t* row = qa.x + r * qa.cols;
+        uint8_t* out = qa.codes + r * qa.cols;
+        RowScale rs;
+        if (nv <= QA_REG_VECS * 32) {
+            uint4 v[QA_REG_VECS];
+            float a = 0.0f;
+#pragma unroll
+            for (int i = 0; i < QA_REG_VECS; ++i) {
+                const int idx = lane + 32 * i;
+                if (idx < nv) v[i] = ld_stream_v4(row + idx * 8);
+            }
+#pragma unroll
+            for (int i = 0; i < QA_REG_VECS; ++i) {
+                const int idx = lane + 32 * i;
+                if (idx < nv)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(v[i], e)));
+            }
+            rs = row_scale<kE4M3>(warp_max_f(a));
+            if (rs.mul) encode_row_vecs<true>(v, QA_REG_VECS, lane, nv, out, rs);
+            else encode_row_vecs<false>(v, QA_REG_VECS, lane, nv, out, rs);
+        } else {
+            // long rows: amax pass, then a second read (from L2) to encode
+            float a = 0.0f;
+            for (int idx0 = 0; idx0 < nv; idx0 += 32 * 8) {
+                uint4 v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int idx = idx0 + lane + 32 * i;
+                    if (idx < nv) v[i] = ld_stream_v4(row + idx * 8);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (idx0 + lane + 32 * i < nv)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(v[i], e)));
+            }
+            rs = row_scale<kE4M3>(warp_max_f(a));
+            for (int idx0 = 0; idx0 < nv; idx0 += 32 * 8) {
+                uint4 v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int idx = idx0 + lane + 32 * i;
+                    if (idx < nv) v[i] = __ldcg(reinterpret_cast<const uint4*>(row) + idx);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int idx = idx0 + lane + 32 * i;
+                    if (idx >= nv) continue;
+                    if (rs.mul) encode_vec<kE4M3, uint16_t, true>(v[i], out + idx * 8, rs);
+                    else encode_vec<kE4M3, uint16_t, false>(v[i], out + idx * 8, rs);
+                }
+            }
+        }
+        if (lane == 0) qa.scales[r] = rs.s;
+    }
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0 && mine) red_add_release_gpu(qa.done, mine);
+}
+// Waits (bounded) until phase 1 has quantized every row.  Called by lane 0 of
+// a warp only (one poller per warp, 256 ns apart, so that the waiting warps do
+// not crowd the L2 slice of the counter while the other CTAs still read their
+// rows); the caller's __syncwarp then orders the other lanes' reads after the
+// acquire.  `tma`: also order this thread's later TMA reads (cross-proxy).
+__device__ __forceinline__ bool qa_wait_all(const QuantA& qa, uint32_t* err, bool tma) {
+    const uint64_t t0 = globaltimer();
+    const uint32_t want = static_cast<uint32_t>(qa.rows);
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.global.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(qa.done) : "memory");
+        if (v >= want) break;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            if (err) atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+        __nanosleep(256);
+    }
+    if (tma) fence_proxy_async_global();
+    return true;
+}
 
 // Reducer side of the fused all-reduce.  A group of AR_WARPS warps (warps 10
 // and 11 of both CTAs of a GEMM pair plus the second CTA's idle warp 1, or
@@ -562,11 +754,13 @@ __device__ __forceinline__ void ar_signal_tiles(const ArParams& ar, uint32_t cnt
 // tile writes 128 columns of silu(g) * u.
 // AR: the kernel carries the reducer warps of the fused all-reduce (ar_job)
 // and, with ar.signal, counts each bf16 output tile on its owner rank.
-template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU, bool AR>
+// QA: the A operand is quantized per row by the kernel itself (phase 1, all
+// warps, before the GEMM roles start; QuantA).
+template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU, bool AR, bool QA = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, SplitTail st,
-               const __grid_constant__ ArParams ar, uint32_t* err) {
+               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, StreamK sk,
+               const __grid_constant__ ArParams ar, const __grid_constant__ QuantA qa, uint32_t* err) {
     static_assert(!AR || OUTK == 1, "the all-reduce signals bf16 tiles");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -591,7 +785,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     const int n_tiles = (N + P_BN - 1) / P_BN;
     const int num_tiles = m_tiles * n_tiles;
     const int kblocks = (K + BK - 1) / BK;
-    const int num_units = st.split > 1 ? st.full_units + st.rem * st.split : num_tiles;
+    const int n_whole = sched_whole(sk, cluster, nclusters);
+    const int n_items = sched_items(sk, kblocks, cluster, nclusters);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
@@ -619,6 +814,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if constexpr (QA) quant_rows_phase(qa, warp, lane, static_cast<int>(blockDim.x >> 5));
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
@@ -627,8 +823,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int u = cluster; u < num_units && ok; u += nclusters) {
-                const Unit un = decode_unit(u, st, kblocks);
+            if constexpr (QA) ok = qa_wait_all(qa, err, true);  // the codes of A are all written
+            for (int j = 0; j < n_items && ok; ++j) {
+                const Unit un = sched_unit(sk, kblocks, cluster, nclusters, n_whole, j);
                 int mb, nb;
                 tile_coords(un.tile, m_tiles, n_tiles, mb, nb);
                 for (int kb = un.kb0; kb < un.kb1; ++kb) {
@@ -657,8 +854,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             uint32_t phase = 0;
             bool ok = true;
             int it = 0;
-            for (int u = cluster; u < num_units && ok; u += nclusters, ++it) {
-                const Unit un = decode_unit(u, st, kblocks);
+            for (int j = 0; j < n_items && ok; ++j, ++it) {
+                const Unit un = sched_unit(sk, kblocks, cluster, nclusters, n_whole, j);
                 const int acc = it & 1;
                 const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err)) { ok = false; break; }
@@ -711,8 +908,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         // complete -- one tile later, so the epilogue never waits on its own stores
         int sig_pending = -1;
         const uint32_t sig_cnt_leader = mapa_shared(smem_u32(sig_cnt), 0);
-        for (int u = cluster; u < num_units; u += nclusters, ++it) {
-            const Unit un = decode_unit(u, st, kblocks);
+        const int w16 = static_cast<int>(rank) * P_EPI_WARPS + (warp - 2);
+        bool qa_ok = true;
+        if constexpr (QA) {
+            // the row scales are all written
+            if (lane == 0) qa_ok = qa_wait_all(qa, err, false);
+            qa_ok = __shfl_sync(0xffffffffu, qa_ok, 0);
+            __syncwarp();
+        }
+        for (int j = 0; j < n_items && __all_sync(0xffffffffu, qa_ok); ++j, ++it) {
+            const Unit un = sched_unit(sk, kblocks, cluster, nclusters, n_whole, j);
             const int tile = un.tile;
             const int acc = it & 1;
             const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
@@ -722,24 +927,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             int mb, nb;
             tile_coords(tile, m_tiles, n_tiles, mb, nb);
             const int row = mb * P_BM + row_in_tile;
-            const bool split_tile = st.split > 1 && tile >= st.full_units;
-            const int slot_id = tile - st.full_units;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * P_BN + colh * 128);
-            // the other K part of a split tile (one partial: split == 2)
-            uint32_t* wsp = split_tile ? st.ws + static_cast<size_t>(slot_id) * (P_BM * P_BN) +
-                                             static_cast<size_t>(row_in_tile) * P_BN + colh * 128
-                                       : nullptr;
-            if (split_tile && un.part > 0) {
-                // part 1 of a tail tile: park the raw accumulators for part 0
+            if (un.park) {
+                // a later part of a tile another cluster finishes: park the raw accumulators
+                uint4* mine = park_slot(sk.ws, cluster, w16);
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + 32u * c, r);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        __stcg(reinterpret_cast<uint4*>(wsp + c * 32 + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+                    for (int q = 0; q < 8; ++q)
+                        __stcg(mine + (c * 8 + q) * 32 + lane, make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]));
                 }
                 tc_fence_before();
                 __threadfence();
@@ -747,17 +947,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 if (lane == 0) {
                     if (rank == 0) mbar_arrive(&tempty[acc]);
                     else mbar_arrive_remote(tempty_leader + 8u * acc);
-                    atomicAdd(st.flags + slot_id, 1u);
+                    atomicAdd(sk.flags + cluster, 1u);
                 }
                 continue;
             }
-            if (split_tile) {
-                // part 0: wait (bounded) until part 1's 16 warps have parked their rows
-                if (lane == 0) wait_flag_geq(st.flags + slot_id, 2u * P_EPI_WARPS, err);
+            const bool fixup = un.c_first <= un.c_last;
+            if (fixup) {
+                // wait (bounded) until the later parts' 16 warps have parked
+                if (lane == 0)
+                    for (int cc = un.c_first; cc <= un.c_last; ++cc) wait_flag_geq(sk.flags + cc, 2u * P_EPI_WARPS, err);
                 __syncwarp();
             }
             const int row0_warp = mb * P_BM + static_cast<int>(rank) * 128 + quarter * 32;
-            const float rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+            float rs;
+            if constexpr (QA) {
+                // the row scales come from phase 1 of this launch (acquired at the top)
+                rs = row < M ? __ldcg(qa.scales + row) : 1.0f;
+            } else {
+                rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+            }
             if constexpr (SWIGLU) {
                 // this warp's 64 output columns: gate TMEM columns colh*64 + [0,64),
                 // up columns 128 + colh*64 + [0,64)
@@ -823,11 +1031,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             int tile_groups = 0;  // bulk store groups this warp commits for this tile
             // this warp's 128 columns, 32 per tcgen05.ld, the next 32 in flight
             uint32_t r[32];
-            uint4 w[8];
+            uint4 w[8];  // the first parked part's next chunk, loaded one chunk ahead
+            const uint4* p0 = fixup ? park_slot(sk.ws, un.c_first, w16) : nullptr;
             tmem_ld_32x32b_x32(taddr, r);
-            if (split_tile) {
+            if (fixup) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp) + j);
+                for (int q = 0; q < 8; ++q) w[q] = __ldcg(p0 + q * 32 + lane);
             }
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
@@ -846,21 +1055,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                         else mbar_arrive_remote(tempty_leader + 8u * acc);
                     }
                 }
-                if (split_tile) {
+                if (fixup) {
+                    // the parked parts, in cluster order (own part first)
+                    add_parked<INT8_KIND>(cur, w);
+                    for (int cc = un.c_first + 1; cc <= un.c_last; ++cc) {
+                        const uint4* pc = park_slot(sk.ws, cc, w16) + c * 8 * 32;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t q[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const int e = 4 * j + t;
-                            if (INT8_KIND) cur[e] = static_cast<uint32_t>(static_cast<int32_t>(cur[e]) + static_cast<int32_t>(q[t]));
-                            else cur[e] = __float_as_uint(__fadd_rn(__uint_as_float(cur[e]), __uint_as_float(q[t])));
-                        }
+                        for (int q = 0; q < 8; ++q) add_parked4<INT8_KIND>(cur, q, __ldcg(pc + q * 32 + lane));
                     }
-                }
-                if (split_tile && c + 1 < 4) {
+                    if (c + 1 < 4) {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) w[j] = __ldcg(reinterpret_cast<const uint4*>(wsp + (c + 1) * 32) + j);
+                        for (int q = 0; q < 8; ++q) w[q] = __ldcg(p0 + ((c + 1) * 8 + q) * 32 + lane);
+                    }
                 }
                 const int col0 = nb * P_BN + colh * 128 + c * 32;
                 if (col0 >= N || row0_warp >= M) continue;
@@ -872,6 +1078,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 if (lane == 0) bulk_wait_group_read<1>();  // the store issued two chunks ago has read this slot
                 __syncwarp();
                 const ColOps cop = col_ops(ep.col_scale, ep.bias, col0, lane, N);
+                // without column scales and bias the per-column operands are
+                // the identities, and skipping them (and their shuffles) gives
+                // the same bits; the branch is warp-uniform
+                const bool plain = !ep.col_scale && !ep.bias;
                 if (OUTK == 1) {
                     // bf16: 64-byte rows, 16-byte chunk j at j ^ ((row >> 1) & 3)
                     uint8_t* rowp = slot + lane * 64;
@@ -882,7 +1092,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                         for (int t = 0; t < 8; ++t) {
                             const int e = 8 * j + t;
                             const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(cur[e])) : __uint_as_float(cur[e]);
-                            v[t] = epi_elem(a, ep.alpha, rs, cop, e);
+                            v[t] = plain ? __fmul_rn(__fmul_rn(a, ep.alpha), rs) : epi_elem(a, ep.alpha, rs, cop, e);
                         }
                         uint4 q;
                         q.x = f32x2_to_bf16x2(v[0], v[1]);
@@ -905,7 +1115,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                             for (int t = 0; t < 4; ++t) {
                                 const int e = 4 * j + t;
                                 const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(cur[e])) : __uint_as_float(cur[e]);
-                                o[t] = __float_as_uint(epi_elem(a, ep.alpha, rs, cop, e));
+                                o[t] = __float_as_uint(plain ? __fmul_rn(__fmul_rn(a, ep.alpha), rs)
+                                                             : epi_elem(a, ep.alpha, rs, cop, e));
                             }
                             q = make_uint4(o[0], o[1], o[2], o[3]);
                         }
@@ -1303,9 +1514,33 @@ nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
     return NQ_SUCCESS;
 }
 
-template <bool I8, bool KN, int OUTK, bool SWIGLU = false, bool AR = false>
+// Stream-K plan of the pair kernel for `tiles` tiles of `kblocks` k-blocks on
+// `clusters` co-resident clusters.  Whole waves stay whole tiles; the last
+// (1 + fraction) waves -- all tiles when there are fewer than two waves --
+// are shared out by k-blocks only when the last wave would be at most half
+// full and K is long (>= 48 k-blocks).  Measured on B200: for shorter K the
+// parking, the flag clear and the in-order fixup waits of the epilogue warps
+// (a short head part waits for its neighbour's long part while holding a
+// TMEM accumulator) cost more than the idle half wave saves -- at 4096^3
+// (3.46 waves, 32 k-blocks) whole tiles are 3-5 us faster.
+StreamK plan_stream_k(int tiles, int kblocks, int clusters, bool allowed) {
+    StreamK p{tiles, 0, nullptr, nullptr};
+    if (!allowed || clusters < 2 || kblocks < 48 || tiles % clusters == 0) return p;
+    if (tiles % clusters > clusters / 2) return p;
+    const int waves = tiles / clusters;
+    const int dp = waves >= 2 ? (waves - 1) * clusters : 0;
+    if (static_cast<long long>(tiles - dp) * kblocks < 4LL * clusters) return p;
+    p.dp_tiles = dp;
+    p.sk_tiles = tiles - dp;
+    return p;
+}
+
+// qap (QA launches): the activations to quantize in phase 1; `a` is then the
+// codes buffer the kernel fills and reads back.
+template <bool I8, bool KN, int OUTK, bool SWIGLU = false, bool AR = false, bool QA = false>
 nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, void* out, const Epi& ep,
-                       cudaStream_t s, const DeviceInfo& di, const ArParams* arp = nullptr) {
+                       cudaStream_t s, const DeviceInfo& di, const ArParams* arp = nullptr,
+                       const QuantA* qap = nullptr) {
     CUtensorMap ma, mb, mc;
     nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, 128);
     if (st != NQ_SUCCESS) return st;
@@ -1321,7 +1556,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     }
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
-    auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU, AR>;
+    auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU, AR, QA>;
     static std::atomic<uint64_t> attr_set{0};
     st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
     if (st != NQ_SUCCESS) return st;
@@ -1341,38 +1576,56 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
         max_clusters[di.device & 63].store(nc, std::memory_order_relaxed);
     }
     const int tiles = ((d.m + P_BM - 1) / P_BM) * ((d.n + P_BN - 1) / P_BN);
-    const int clusters = std::max(1, std::min(tiles, max_clusters[di.device & 63].load(std::memory_order_relaxed)));
+    const int kblocks = (d.k + BK - 1) / BK;
+    const int resident = std::max(1, max_clusters[di.device & 63].load(std::memory_order_relaxed));
+    const StreamK plan = plan_stream_k(tiles, kblocks, resident, !SWIGLU && !AR);
+    // a QA launch quantizes A on every resident cluster, whatever its tile count
+    const int clusters = (plan.sk_tiles > 0 || QA) ? resident : std::max(1, std::min(tiles, resident));
     constexpr int threads = AR ? P_THREADS_AR : P_THREADS;
     const int grid = 2 * clusters;
-    const int kblocks = (d.k + BK - 1) / BK;
-    SplitTail tail{tiles, 0, 1, nullptr, nullptr};
-    const int rem = tiles % clusters;
-    // Splitting pays off only when a tile's MMA time clearly exceeds its
-    // epilogue (part 0's epilogue waits for part 1's): long K only.
-    const int split = (!SWIGLU && !AR && rem && clusters / rem >= 2 && kblocks >= 48) ? 2 : 1;
+    StreamK sk = plan;
     void* scratch = nullptr;
-    if (split >= 2) {
-        tail.full_units = tiles - rem;
-        tail.rem = rem;
-        tail.split = split;
-        const size_t ws_bytes = static_cast<size_t>(rem) * P_BM * P_BN * 4;
-        st = scratch_alloc(&scratch, ws_bytes + 256 * ((rem * 4 + 255) / 256), s);
+    if (sk.sk_tiles > 0) {
+        // one 256 x 256 accumulator slot and one flag per cluster
+        const size_t ws_bytes = static_cast<size_t>(clusters) * P_BM * P_BN * 4;
+        st = scratch_alloc(&scratch, ws_bytes + 256 * ((clusters * 4 + 255) / 256), s);
         if (st != NQ_SUCCESS) return st;
-        tail.ws = static_cast<uint32_t*>(scratch);
-        tail.flags = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + ws_bytes);
-        cudaError_t e = cudaMemsetAsync(tail.flags, 0, sizeof(uint32_t) * rem, s);
+        sk.ws = static_cast<uint32_t*>(scratch);
+        sk.flags = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + ws_bytes);
+        cudaError_t e = cudaMemsetAsync(sk.flags, 0, sizeof(uint32_t) * clusters, s);
         if (e != cudaSuccess) {
             scratch_free(scratch, s);
-            return cuda_status(e, "nq_gemm: clear split flags");
+            return cuda_status(e, "nq_gemm: clear stream-K flags");
+        }
+    }
+    QuantA qa;
+    std::memset(&qa, 0, sizeof(qa));
+    void* qa_flags = nullptr;
+    if (QA) {
+        // the count of quantized rows, zero before the launch
+        qa = *qap;
+        const size_t fb = sizeof(uint32_t);
+        st = scratch_alloc(&qa_flags, 256, s);
+        if (st != NQ_SUCCESS) {
+            if (scratch) scratch_free(scratch, s);
+            return st;
+        }
+        qa.done = static_cast<uint32_t*>(qa_flags);
+        cudaError_t e = cudaMemsetAsync(qa.done, 0, fb, s);
+        if (e != cudaSuccess) {
+            scratch_free(qa_flags, s);
+            if (scratch) scratch_free(scratch, s);
+            return cuda_status(e, "nq_gemm: clear row-block flags");
         }
     }
     uint32_t* err = device_error_word();
     ArParams ar;
     if (arp) ar = *arp;
     else std::memset(&ar, 0, sizeof(ar));
-    kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, tail, ar, err);
+    kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, sk, ar, qa, err);
     cudaError_t e = cudaGetLastError();
     if (scratch) scratch_free(scratch, s);
+    if (qa_flags) scratch_free(qa_flags, s);
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
 }
 
@@ -1628,6 +1881,44 @@ nq_status_t gemm_allreduce_impl(const nq_gemm_desc_t* d, const nq_allreduce_desc
               : launch_tc2<false, false, 1, false, true>(*d, a, b, out, ep, s, di, &ar);
 }
 
+// GEMM whose A operand is per-token quantized inside the kernel (QuantA).
+nq_status_t gemm_quant_a_impl(const nq_gemm_desc_t* d, const void* x, uint8_t* a_codes, float* a_scales,
+                              const void* b, void* out, cudaStream_t s) {
+    if (!d) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_quant_a: null descriptor");
+    if (d->m < 0 || d->n < 0 || d->k < 0) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_quant_a: negative size");
+    if (d->m == 0 || d->n == 0) return NQ_SUCCESS;
+    if (!x || !a_codes || !a_scales || !b || !out) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_quant_a: null pointer");
+    if (d->a_format != NQ_E4M3 || (d->b_format != NQ_E4M3 && d->b_format != NQ_E5M2))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_quant_a: A is quantized to E4M3; B must be E4M3 or E5M2");
+    if (d->b_layout != NQ_B_KN && d->b_layout != NQ_B_NK) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_quant_a: b_layout");
+    if (d->row_scale) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_quant_a: row_scale must be NULL (the kernel's per-token scales are used)");
+    if (d->out_dtype != NQ_BF16 && d->out_dtype != NQ_F32) return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_quant_a: f32 or bf16 output");
+    if (d->epilogue != NQ_EPI_NONE && d->epilogue != NQ_EPI_SWIGLU) return fail(NQ_ERROR_INVALID_VALUE, "nq_gemm_quant_a: epilogue");
+    const bool swiglu = d->epilogue == NQ_EPI_SWIGLU;
+    if (swiglu && d->n % P_BN != 0) return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_quant_a: SwiGLU needs n % 256 == 0");
+    if (d->k == 0 || d->k % 16 != 0 || d->n % 16 != 0 || !aligned16(x) || !aligned16(a_codes) || !aligned16(b) ||
+        !aligned16(out))
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm_quant_a: needs k, n % 16 == 0 and 16-byte aligned pointers");
+    DeviceInfo di;
+    nq_status_t st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    Epi ep{out, swiglu ? d->n / 2 : d->n, d->out_dtype, d->alpha, a_scales, d->col_scale, d->bias};
+    QuantA qa{static_cast<const uint16_t*>(x), a_codes, a_scales, nullptr, d->m, d->k};
+    const bool kn = d->b_layout == NQ_B_KN;
+    if (swiglu) {
+        if (d->out_dtype == NQ_BF16)
+            return kn ? launch_tc2<false, true, 1, true, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa)
+                      : launch_tc2<false, false, 1, true, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa);
+        return kn ? launch_tc2<false, true, 0, true, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa)
+                  : launch_tc2<false, false, 0, true, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa);
+    }
+    if (d->out_dtype == NQ_BF16)
+        return kn ? launch_tc2<false, true, 1, false, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa)
+                  : launch_tc2<false, false, 1, false, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa);
+    return kn ? launch_tc2<false, true, 0, false, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa)
+              : launch_tc2<false, false, 0, false, false, true>(*d, a_codes, b, out, ep, s, di, nullptr, &qa);
+}
+
 nq_status_t allreduce_finish_impl(const nq_allreduce_desc_t* r, cudaStream_t s) {
     ArParams ar;
     nq_status_t st = fill_ar(r, &ar);
@@ -1669,6 +1960,11 @@ nq_status_t nq_gemm_allreduce(const nq_gemm_desc_t* d, const nq_allreduce_desc_t
 
 nq_status_t nq_allreduce_finish(const nq_allreduce_desc_t* a_r, nq_stream_t s) {
     return nq::allreduce_finish_impl(a_r, s);
+}
+
+nq_status_t nq_gemm_quant_a(const nq_gemm_desc_t* desc, const void* x, uint8_t* a_codes, float* a_scales,
+                            const void* b, void* out, nq_stream_t s) {
+    return nq::gemm_quant_a_impl(desc, x, a_codes, a_scales, b, out, s);
 }
 
 // Test hook: the same GEMM forced onto the SIMT kernel (exact sequential-k).

@@ -206,46 +206,11 @@ __global__ void __launch_bounds__(kThreads) k_histogram(const float* __restrict_
     }
 }
 
-// Per-row / per-column scaling: scale = amax / qmax (1 for an all-zero row)
-// and q = encode(x * inv) with inv = qmax / amax, one IEEE division per row.
-// When qmax / amax overflows (amax < qmax / FLT_MAX) the row is divided by
-// its scale instead, so a row of tiny values never meets an infinite
-// multiplier.  The choice is uniform over a row, so it costs no divergence.
-struct RowScale {
-    float s, inv;
-    bool mul;
-};
-template <int F>
-__device__ __forceinline__ RowScale row_scale(float a) {
-    constexpr float q = dev::FmtTraits<F>::qmax;
-    if (!(a > 0.0f)) return RowScale{1.0f, 1.0f, true};
-    const float inv = q / a;
-    return RowScale{a / q, inv, inv <= FLT_MAX};
-}
-template <bool MUL>
-__device__ __forceinline__ float scale_apply(float x, const RowScale& r) {
-    return MUL ? x * r.inv : x / r.s;
-}
-
-// Element e of a 16-byte vector of fp32 (4) or bf16 (8) values.
-template <class In>
-__device__ __forceinline__ float vec_elem(const uint4& q, int e) {
-    constexpr int EPV = 16 / sizeof(In);
-    const uint32_t w = e < EPV / 4 ? q.x : (e < EPV / 2 ? q.y : (e < 3 * EPV / 4 ? q.z : q.w));
-    if (sizeof(In) == 2) return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
-    return __uint_as_float(w);
-}
-template <int F, class In, bool MUL>
-__device__ __forceinline__ void encode_vec(const uint4& q, uint8_t* out, const RowScale& r) {
-    constexpr int EPV = 16 / sizeof(In);
-    uint32_t codes[EPV / 2];
-#pragma unroll
-    for (int e = 0; e < EPV; e += 2)
-        codes[e / 2] = dev::ocp_encode2<F>(scale_apply<MUL>(vec_elem<In>(q, e), r),
-                                           scale_apply<MUL>(vec_elem<In>(q, e + 1), r));
-    if (EPV == 8) *reinterpret_cast<uint2*>(out) = make_uint2(codes[0] | (codes[1] << 16), codes[2] | (codes[3] << 16));
-    else *reinterpret_cast<uint32_t*>(out) = codes[0] | (codes[1] << 16);
-}
+using dev::encode_vec;
+using dev::row_scale;
+using dev::RowScale;
+using dev::scale_apply;
+using dev::vec_elem;
 
 // Per-row scaled quantize, any width and alignment: one block per row; the
 // second pass re-reads the row (from L1/L2).
