@@ -492,15 +492,20 @@ constexpr int P_SMEM_BYTES = 1024 + P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_B
 
 // A operand quantized inside the GEMM (per-token dynamic quantization fused
 // into the kernel): bf16 activations x (rows x cols), their E4M3 codes and
-// per-row scales written by phase 1, and the count of rows done.
+// per-row scales.  Rows [0, head) -- the first band of M-tiles, all the first
+// waves of tiles need -- are quantized by every warp of the grid before the
+// GEMM roles start (phase 1a); rows [head, rows) by the epilogue warps while
+// the first tiles' MMAs run (phase 1b).  done[0] / done[1] count the rows of
+// each part.
 struct QuantA {
     const uint16_t* x;
     uint8_t* codes;
     float* scales;
-    uint32_t* done;  // rows quantized so far; zero before the launch
+    uint32_t* done;  // [2], zero before the launch
     int rows, cols;
+    int head;        // rows of phase 1a
 };
-constexpr int QA_REG_VECS = 16;  // rows up to 16 * 32 * 8 = 4096 values stay in registers
+constexpr int QA_REG_VECS = 16;  // rows up to 16 * 32 * 8 = 4096 values fit in registers
 
 __device__ __forceinline__ float warp_max_f(float v) {
 #pragma unroll
@@ -517,104 +522,172 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
 __device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-template <bool MUL>
-__device__ __forceinline__ void encode_row_vecs(const uint4* v, int n, int lane, int nv, uint8_t* out,
+// Codes of the 8-value vectors idx = lane + 32 i (i < n) of a row, from v[].
+template <bool MUL, int NV>
+__device__ __forceinline__ void encode_row_vecs(const uint4 (&v)[NV], int n, int lane, int nv, uint8_t* out,
                                                 const RowScale& rs) {
 #pragma unroll
-    for (int i = 0; i < QA_REG_VECS; ++i) {
+    for (int i = 0; i < NV; ++i) {
         const int idx = lane + 32 * i;
         if (i < n && idx < nv) encode_vec<kE4M3, uint16_t, MUL>(v[i], out + idx * 8, rs);
     }
 }
-// Phase 1: warp w of the grid takes rows w, w + nw, ...: the row's amax, its
-// codes q = E4M3(x * (448 / amax)) and scale amax / 448 -- the arithmetic of
-// nq_quantize_rows, bit for bit.  When its rows are written the warp counts
-// them on qa.done (a release, after a proxy fence: TMA reads the codes back).
-// The GEMM roles then wait once for all rows (qa_wait_all): one acquire and
-// one cross-proxy fence per thread, instead of one per tile, which stalled
-// the TMA producer between tiles.
-__device__ void quant_rows_phase(const QuantA& qa, int warp, int lane, int warps_per_cta) {
-    const int nv = qa.cols / 8;
-    const long long nw = static_cast<long long>(gridDim.x) * warps_per_cta;
-    uint32_t mine = 0;
-    for (long long r = static_cast<long long>(blockIdx.x) * warps_per_cta + warp; r < qa.rows; r += nw, ++mine) {
-        const uint16_t* row = qa.x + r * qa.cols;
-        uint8_t* out = qa.codes + r * qa.cols;
-        RowScale rs;
-        if (nv <= QA_REG_VECS * 32) {
-            uint4 v[QA_REG_VECS];
-            float a = 0.0f;
+// One row from global memory: in registers when it has at most 4096 values,
+// else an amax pass and an encode pass (the second read hits L2).  Returns
+// the row's scale; the codes are stored to `out`.  The arithmetic of
+// nq_quantize_rows, bit for bit.
+__device__ float quant_row_global(const uint16_t* row, uint8_t* out, int nv, int lane) {
+    RowScale rs;
+    if (nv <= QA_REG_VECS * 32) {
+        uint4 v[QA_REG_VECS];
+        float a = 0.0f;
 #pragma unroll
-            for (int i = 0; i < QA_REG_VECS; ++i) {
-                const int idx = lane + 32 * i;
-                if (idx < nv) v[i] = ld_stream_v4(row + idx * 8);
-            }
-#pragma unroll
-            for (int i = 0; i < QA_REG_VECS; ++i) {
-                const int idx = lane + 32 * i;
-                if (idx < nv)
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(v[i], e)));
-            }
-            rs = row_scale<kE4M3>(warp_max_f(a));
-            if (rs.mul) encode_row_vecs<true>(v, QA_REG_VECS, lane, nv, out, rs);
-            else encode_row_vecs<false>(v, QA_REG_VECS, lane, nv, out, rs);
-        } else {
-            // long rows: amax pass, then a second read (from L2) to encode
-            float a = 0.0f;
-            for (int idx0 = 0; idx0 < nv; idx0 += 32 * 8) {
-                uint4 v[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int idx = idx0 + lane + 32 * i;
-                    if (idx < nv) v[i] = ld_stream_v4(row + idx * 8);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    if (idx0 + lane + 32 * i < nv)
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(v[i], e)));
-            }
-            rs = row_scale<kE4M3>(warp_max_f(a));
-            for (int idx0 = 0; idx0 < nv; idx0 += 32 * 8) {
-                uint4 v[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int idx = idx0 + lane + 32 * i;
-                    if (idx < nv) v[i] = __ldcg(reinterpret_cast<const uint4*>(row) + idx);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int idx = idx0 + lane + 32 * i;
-                    if (idx >= nv) continue;
-                    if (rs.mul) encode_vec<kE4M3, uint16_t, true>(v[i], out + idx * 8, rs);
-                    else encode_vec<kE4M3, uint16_t, false>(v[i], out + idx * 8, rs);
-                }
-            }
+        for (int i = 0; i < QA_REG_VECS; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < nv) v[i] = ld_stream_v4(row + idx * 8);
         }
-        if (lane == 0) qa.scales[r] = rs.s;
+#pragma unroll
+        for (int i = 0; i < QA_REG_VECS; ++i)
+            if (lane + 32 * i < nv)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(v[i], e)));
+        rs = row_scale<kE4M3>(warp_max_f(a));
+        if (rs.mul) encode_row_vecs<true>(v, QA_REG_VECS, lane, nv, out, rs);
+        else encode_row_vecs<false>(v, QA_REG_VECS, lane, nv, out, rs);
+        return rs.s;
     }
+    float a = 0.0f;
+    for (int idx0 = 0; idx0 < nv; idx0 += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = idx0 + lane + 32 * i;
+            if (idx < nv) v[i] = ld_stream_v4(row + idx * 8);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (idx0 + lane + 32 * i < nv)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(v[i], e)));
+    }
+    rs = row_scale<kE4M3>(warp_max_f(a));
+    for (int idx0 = 0; idx0 < nv; idx0 += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = idx0 + lane + 32 * i;
+            if (idx < nv) v[i] = __ldcg(reinterpret_cast<const uint4*>(row) + idx);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = idx0 + lane + 32 * i;
+            if (idx >= nv) continue;
+            if (rs.mul) encode_vec<kE4M3, uint16_t, true>(v[i], out + idx * 8, rs);
+            else encode_vec<kE4M3, uint16_t, false>(v[i], out + idx * 8, rs);
+        }
+    }
+    return rs.s;
+}
+// Counts `mine` finished rows on *done once the warp's codes and scales are
+// written: a release after a proxy fence (TMA reads the codes back).
+__device__ __forceinline__ void qa_publish(uint32_t* done, uint32_t mine, int lane) {
     fence_proxy_async_global();
     __syncwarp();
-    if (lane == 0 && mine) red_add_release_gpu(qa.done, mine);
+    if (lane == 0 && mine) red_add_release_gpu(done, mine);
 }
-// Waits (bounded) until phase 1 has quantized every row.  Called by lane 0 of
-// a warp only (one poller per warp, 256 ns apart, so that the waiting warps do
-// not crowd the L2 slice of the counter while the other CTAs still read their
-// rows); the caller's __syncwarp then orders the other lanes' reads after the
-// acquire.  `tma`: also order this thread's later TMA reads (cross-proxy).
-__device__ __forceinline__ bool qa_wait_all(const QuantA& qa, uint32_t* err, bool tma) {
-    const uint64_t t0 = globaltimer();
-    const uint32_t want = static_cast<uint32_t>(qa.rows);
-    while (true) {
-        uint32_t v;
-        asm volatile("ld.global.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(qa.done) : "memory");
-        if (v >= want) break;
-        if (globaltimer() - t0 > kWaitLimitNs) {
-            if (err) atomicOr(err, kErrWaitTimeout);
-            return false;
+// Phase 1a: rows [0, qa.head) over every warp of the grid.  Each warp's rows
+// stream through its slice of the CTA's shared memory (still unused by the
+// GEMM) with cp.async, `stages` rows in flight; every lane reads back only
+// the 16-byte pieces it copied itself, so no barrier is needed between the
+// copy and the use.  Rows that do not fit the slice take quant_row_global.
+__device__ void quant_rows_head(const QuantA& qa, int warp, int lane, int warps_per_cta, uint8_t* smem,
+                                uint32_t smem_bytes) {
+    const int nv = qa.cols / 8;
+    const uint32_t rb = static_cast<uint32_t>(qa.cols) * 2;
+    const uint32_t slice = (smem_bytes / warps_per_cta) & ~15u;
+    const int stages = static_cast<int>(min(4u, slice / rb));
+    const long long nw = static_cast<long long>(gridDim.x) * warps_per_cta;
+    const long long r0 = static_cast<long long>(blockIdx.x) * warps_per_cta + warp;
+    uint32_t mine = 0;
+    if (stages < 1) {
+        for (long long r = r0; r < qa.head; r += nw, ++mine) {
+            const float sc = quant_row_global(qa.x + r * qa.cols, qa.codes + r * qa.cols, nv, lane);
+            if (lane == 0) qa.scales[r] = sc;
         }
-        __nanosleep(256);
+        qa_publish(qa.done, mine, lane);
+        return;
+    }
+    uint8_t* ring = smem + static_cast<size_t>(warp) * slice;
+    auto issue = [&](long long r, int st) {
+        if (r < qa.head) {
+            const uint4* src = reinterpret_cast<const uint4*>(qa.x + r * qa.cols);
+            uint4* dst = reinterpret_cast<uint4*>(ring + static_cast<size_t>(st) * rb);
+            for (int idx = lane; idx < nv; idx += 32) cp_async_16(dst + idx, src + idx);
+        }
+        cp_async_commit();  // an empty group past the last row keeps the count uniform
+    };
+    for (int st = 0; st < stages; ++st) issue(r0 + st * nw, st);
+    int st = 0;
+    for (long long r = r0; r < qa.head; r += nw, ++mine) {
+        // the oldest group (this row) has landed once at most stages-1 remain
+        switch (stages) {
+            case 1: cp_async_wait<0>(); break;
+            case 2: cp_async_wait<1>(); break;
+            case 3: cp_async_wait<2>(); break;
+            default: cp_async_wait<3>(); break;
+        }
+        const uint4* buf = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(st) * rb);
+        float a = 0.0f;
+        for (int idx = lane; idx < nv; idx += 32) {
+            const uint4 q = buf[idx];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(vec_elem<uint16_t>(q, e)));
+        }
+        const RowScale rs = row_scale<kE4M3>(warp_max_f(a));
+        uint8_t* out = qa.codes + r * qa.cols;
+        if (rs.mul)
+            for (int idx = lane; idx < nv; idx += 32) encode_vec<kE4M3, uint16_t, true>(buf[idx], out + idx * 8, rs);
+        else
+            for (int idx = lane; idx < nv; idx += 32) encode_vec<kE4M3, uint16_t, false>(buf[idx], out + idx * 8, rs);
+        if (lane == 0) qa.scales[r] = rs.s;
+        issue(r + static_cast<long long>(stages) * nw, st);  // this lane's pieces of buffer st are consumed
+        if (++st == stages) st = 0;
+    }
+    cp_async_wait<0>();
+    qa_publish(qa.done, mine, lane);
+}
+// Phase 1b: rows [qa.head, qa.rows) over the grid's epilogue warps (ew of
+// new_w), from global memory.
+__device__ void quant_rows_tail(const QuantA& qa, int ew, int new_w, int lane) {
+    const int nv = qa.cols / 8;
+    const long long nw = static_cast<long long>(gridDim.x) * new_w;
+    uint32_t mine = 0;
+    for (long long r = qa.head + static_cast<long long>(blockIdx.x) * new_w + ew; r < qa.rows; r += nw, ++mine) {
+        const float sc = quant_row_global(qa.x + r * qa.cols, qa.codes + r * qa.cols, nv, lane);
+        if (lane == 0) qa.scales[r] = sc;
+    }
+    qa_publish(qa.done + 1, mine, lane);
+}
+// Waits (bounded) until the rows of part `part` (0: [0, head), 1: the rest)
+// are all quantized.  Called by lane 0 of a warp only (one poller per warp,
+// 256 ns apart, so waiting warps do not crowd the counter's L2 slice while
+// other CTAs still read their rows); the caller's __syncwarp orders the other
+// lanes' reads after the acquire.  `tma`: also order this thread's later TMA
+// reads (cross-proxy).
+__device__ __forceinline__ bool qa_wait(const QuantA& qa, int part, uint32_t* err, bool tma) {
+    const uint32_t want = static_cast<uint32_t>(part == 0 ? qa.head : qa.rows - qa.head);
+    if (want) {
+        const uint64_t t0 = globaltimer();
+        while (true) {
+            uint32_t v;
+            asm volatile("ld.global.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(qa.done + part) : "memory");
+            if (v >= want) break;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                if (err) atomicOr(err, kErrWaitTimeout);
+                return false;
+            }
+            __nanosleep(256);
+        }
     }
     if (tma) fence_proxy_async_global();
     return true;
@@ -814,7 +887,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    if constexpr (QA) quant_rows_phase(qa, warp, lane, static_cast<int>(blockDim.x >> 5));
+    if constexpr (QA) {
+        // phase 1a through the operand ring and staging slots, then hand them
+        // to TMA: the generic reads of this shared memory come before the
+        // producer's async-proxy writes
+        quant_rows_head(qa, warp, lane, static_cast<int>(blockDim.x >> 5), smem,
+                        static_cast<uint32_t>(P_STAGES * (P_A_STAGE + P_B_STAGE) + P_EPI_BYTES));
+        fence_proxy_async_smem();
+        __syncthreads();
+    }
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
@@ -823,11 +904,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            if constexpr (QA) ok = qa_wait_all(qa, err, true);  // the codes of A are all written
+            int qa_part = -1;  // QA: the last part of A's rows seen complete
             for (int j = 0; j < n_items && ok; ++j) {
                 const Unit un = sched_unit(sk, kblocks, cluster, nclusters, n_whole, j);
                 int mb, nb;
                 tile_coords(un.tile, m_tiles, n_tiles, mb, nb);
+                if constexpr (QA) {
+                    // rows of this tile (both CTAs') quantized: a wait and a fence per part
+                    const int part = (mb + 1) * P_BM > qa.head ? 1 : 0;
+                    if (part > qa_part) {
+                        for (int q = qa_part + 1; q <= part && ok; ++q) ok = qa_wait(qa, q, err, true);
+                        if (!ok) break;
+                        qa_part = part;
+                    }
+                }
                 for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
                     if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_STAGE + P_B_STAGE));
@@ -909,14 +999,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         int sig_pending = -1;
         const uint32_t sig_cnt_leader = mapa_shared(smem_u32(sig_cnt), 0);
         const int w16 = static_cast<int>(rank) * P_EPI_WARPS + (warp - 2);
-        bool qa_ok = true;
-        if constexpr (QA) {
-            // the row scales are all written
-            if (lane == 0) qa_ok = qa_wait_all(qa, err, false);
-            qa_ok = __shfl_sync(0xffffffffu, qa_ok, 0);
-            __syncwarp();
-        }
-        for (int j = 0; j < n_items && __all_sync(0xffffffffu, qa_ok); ++j, ++it) {
+        int qa_part = -1;  // QA: the last part of A's rows whose scales this warp acquired
+        // QA: the rows past the head, before this warp's first epilogue (the MMAs of
+        // the first tiles run meanwhile)
+        if constexpr (QA) quant_rows_tail(qa, warp - 2, P_EPI_WARPS, lane);
+        for (int j = 0; j < n_items; ++j, ++it) {
             const Unit un = sched_unit(sk, kblocks, cluster, nclusters, n_whole, j);
             const int tile = un.tile;
             const int acc = it & 1;
@@ -926,6 +1013,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             tc_fence_after();
             int mb, nb;
             tile_coords(tile, m_tiles, n_tiles, mb, nb);
+            if constexpr (QA) {
+                // the row scales of this tile come from phase 1 of this launch
+                const int part = (mb + 1) * P_BM > qa.head ? 1 : 0;
+                if (part > qa_part) {
+                    if (lane == 0)
+                        for (int q = qa_part + 1; q <= part; ++q) qa_wait(qa, q, err, false);
+                    __syncwarp();
+                    qa_part = part;
+                }
+            }
             const int row = mb * P_BM + row_in_tile;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * P_BN + colh * 128);
@@ -1604,7 +1701,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     if (QA) {
         // the count of quantized rows, zero before the launch
         qa = *qap;
-        const size_t fb = sizeof(uint32_t);
+        const size_t fb = 2 * sizeof(uint32_t);
         st = scratch_alloc(&qa_flags, 256, s);
         if (st != NQ_SUCCESS) {
             if (scratch) scratch_free(scratch, s);
@@ -1903,7 +2000,9 @@ nq_status_t gemm_quant_a_impl(const nq_gemm_desc_t* d, const void* x, uint8_t* a
     nq_status_t st = current_device(&di);
     if (st != NQ_SUCCESS) return st;
     Epi ep{out, swiglu ? d->n / 2 : d->n, d->out_dtype, d->alpha, a_scales, d->col_scale, d->bias};
-    QuantA qa{static_cast<const uint16_t*>(x), a_codes, a_scales, nullptr, d->m, d->k};
+    // the first band of M-tiles (the rows the first waves of tiles need) is
+    // quantized before the GEMM starts, the rest by the epilogue warps
+    QuantA qa{static_cast<const uint16_t*>(x), a_codes, a_scales, nullptr, d->m, d->k, std::min(d->m, P_BAND * P_BM)};
     const bool kn = d->b_layout == NQ_B_KN;
     if (swiglu) {
         if (d->out_dtype == NQ_BF16)
