@@ -125,6 +125,11 @@ nq_status_t nq_fake_quantize_int8(const float* src, float* dst, size_t n, float 
 nq_status_t nq_quantize_f32_to_int8_round_away(const float* src, int8_t* dst, size_t n,
                                                float scale, nq_stream_t s);
 
+/* dst = (float)src for n bf16 values (exact).  No reference counterpart: the
+   drop-in TP layers return the bf16 output of the fused all-reduce as the fp32
+   the reference's forward(float*) writes. */
+nq_status_t nq_convert_bf16_to_f32(const void* src, float* dst, size_t n, nq_stream_t s);
+
 /* ---- reductions and calibration ----------------------------------------------
  * int8_kernels.hpp:88-92 (int8_kernels.cu:324-410).  `data` may be host or
  * device memory, as may `min_val` / `max_val`.  Synchronises `s`.  NaNs are

@@ -101,9 +101,11 @@ def build_cpp_tests() -> None:
         for d, _, fs in os.walk(os.path.join(ROOT, "include")):
             hdrs += [os.path.join(d, f) for f in fs]
         if _newer([src, LIB] + hdrs, exe):
+            # the TP layers' context holds NCCL communicators
+            nccl = ["-lnccl", "-pthread"] if "nccl" in open(src).read() else []
             _run(["g++", "-std=c++17", "-O2", "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include",
                   src, "-o", exe, "-L", HERE, "-lnova_q", f"-Wl,-rpath,{HERE}", "-L", "/usr/local/cuda/lib64",
-                  "-lcudart", f"-Wl,-rpath,/usr/local/cuda/lib64"])
+                  "-lcudart", f"-Wl,-rpath,/usr/local/cuda/lib64"] + nccl)
 
 
 def build_all(verbose: bool = False) -> None:

@@ -77,6 +77,7 @@ _SIGS = {
     "nq_gemm": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_gemm_simt": [C.POINTER(GemmDesc), _p, _p, _p, _p],
     "nq_gemm_quant_a": [C.POINTER(GemmDesc), _p, _p, _p, _p, _p, _p],
+    "nq_convert_bf16_to_f32": [_p, _p, _sz, _p],
     "nq_gemm_allreduce": [C.POINTER(GemmDesc), C.POINTER(AllreduceDesc), _p, _p, _p, _p],
     "nq_allreduce_finish": [C.POINTER(AllreduceDesc), _p],
     "nq_fp8_gemm_forward": [_p, _p, _p, _i, _i, _i, _f, _f, _f, _p],

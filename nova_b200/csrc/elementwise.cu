@@ -328,6 +328,23 @@ __global__ void __launch_bounds__(256) k_fp8_act(const uint8_t* __restrict__ src
         dst[i] = static_cast<uint8_t>(fp8_act1<E4M3, OP>(__ldg(src + i), alpha));
 }
 
+// bf16 -> fp32, 8 values per thread step when both pointers are 16-byte aligned.
+__global__ void __launch_bounds__(256) k_bf16_to_f32(const uint16_t* __restrict__ src, float* __restrict__ dst,
+                                                     size_t n, int vec) {
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t n8 = vec ? n / 8 : 0;
+    for (size_t v = t0; v < n8; v += stride) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(src) + v);
+        float4* o = reinterpret_cast<float4*>(dst) + 2 * v;
+        o[0] = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
+                           __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u));
+        o[1] = make_float4(__uint_as_float(q.z << 16), __uint_as_float(q.z & 0xFFFF0000u),
+                           __uint_as_float(q.w << 16), __uint_as_float(q.w & 0xFFFF0000u));
+    }
+    for (size_t i = n8 * 8 + t0; i < n; i += stride) dst[i] = __uint_as_float(static_cast<uint32_t>(__ldg(src + i)) << 16);
+}
+
 // ---- launch helpers ------------------------------------------------------------------
 nq_status_t grid_for(size_t n, int* grid) {
     DeviceInfo di;
@@ -537,6 +554,18 @@ nq_status_t nq_dequantize_scaled(const uint8_t* src, float* dst, size_t n, nq_fo
         default: return fail(NQ_ERROR_INVALID_VALUE, "nq_dequantize_scaled: format");
     }
     NQ_LAUNCH_CHECK("nq_dequantize_scaled");
+    return NQ_SUCCESS;
+}
+
+nq_status_t nq_convert_bf16_to_f32(const void* src, float* dst, size_t n, nq_stream_t s) {
+    if (n == 0) return NQ_SUCCESS;
+    if (!src || !dst) return fail(NQ_ERROR_INVALID_VALUE, "nq_convert_bf16_to_f32: null pointer");
+    int grid;
+    nq_status_t st = nq::grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    const int vec = nq::aligned16(src) && nq::aligned16(dst);
+    nq::k_bf16_to_f32<<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(src), dst, n, vec);
+    NQ_LAUNCH_CHECK("nq_convert_bf16_to_f32");
     return NQ_SUCCESS;
 }
 
