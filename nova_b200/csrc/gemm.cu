@@ -362,16 +362,22 @@ constexpr int P_B_STAGE = 128 * BK;  // 16 KB per CTA
 // finishing cluster adds the parked parts in cluster order before its
 // epilogue: deterministic, exact for int32.  A cluster parks at most once
 // (only its first stream-K item can start inside a tile).
+// Half tiles: when the last wave of whole tiles would fill at most half the
+// clusters, each of its `half_tiles` tiles is computed as two 256 x 128
+// halves (tcgen05.mma N = 128) on two clusters instead, so the tail takes
+// half a tile's time and needs no cross-cluster fixup.  Excludes stream-K.
 struct StreamK {
     int dp_tiles;     // whole tiles, round-robin
     int sk_tiles;     // tiles whose k-blocks are shared out (0: none)
     uint32_t* ws;     // [clusters][256 x 256] parked accumulators
     uint32_t* flags;  // [clusters] epilogue warps that parked
+    int half_tiles;   // tiles [dp_tiles, dp_tiles + half_tiles) done as two 256 x 128 halves
 };
 struct Unit {
     int tile, kb0, kb1;
     int park;            // the accumulators go to this cluster's workspace slot
     int c_first, c_last; // the tile's later parts, parked by these clusters (none if c_first > c_last)
+    int half;            // 0: the whole tile; 1 / 2: its columns [0, 128) / [128, 256)
 };
 __host__ __device__ __forceinline__ long long sk_begin(long long total, int c, int nclusters) {
     return total * c / nclusters;
@@ -383,6 +389,7 @@ __device__ __forceinline__ int sched_whole(const StreamK& sk, int cluster, int n
 }
 __device__ __forceinline__ int sched_items(const StreamK& sk, int kblocks, int cluster, int nclusters) {
     int n = sched_whole(sk, cluster, nclusters);
+    if (sk.half_tiles > 0 && cluster < 2 * sk.half_tiles) n += (2 * sk.half_tiles - cluster + nclusters - 1) / nclusters;
     if (sk.sk_tiles > 0) {
         const long long total = static_cast<long long>(sk.sk_tiles) * kblocks;
         const long long b0 = sk_begin(total, cluster, nclusters), b1 = sk_begin(total, cluster + 1, nclusters);
@@ -392,7 +399,11 @@ __device__ __forceinline__ int sched_items(const StreamK& sk, int kblocks, int c
 }
 __device__ __forceinline__ Unit sched_unit(const StreamK& sk, int kblocks, int cluster, int nclusters, int n_whole,
                                            int j) {
-    if (j < n_whole) return Unit{cluster + j * nclusters, 0, kblocks, 0, 1, 0};
+    if (j < n_whole) return Unit{cluster + j * nclusters, 0, kblocks, 0, 1, 0, 0};
+    if (sk.half_tiles > 0) {
+        const int hu = cluster + (j - n_whole) * nclusters;
+        return Unit{sk.dp_tiles + hu / 2, 0, kblocks, 0, 1, 0, 1 + (hu & 1)};
+    }
     const long long total = static_cast<long long>(sk.sk_tiles) * kblocks;
     const long long b0 = sk_begin(total, cluster, nclusters), b1 = sk_begin(total, cluster + 1, nclusters);
     const long long lt = b0 / kblocks + (j - n_whole);
@@ -402,6 +413,7 @@ __device__ __forceinline__ Unit sched_unit(const StreamK& sk, int kblocks, int c
     u.kb0 = static_cast<int>((b0 > t0 ? b0 : t0) - t0);
     u.kb1 = static_cast<int>((b1 < t1 ? b1 : t1) - t0);
     u.park = u.kb0 > 0;
+    u.half = 0;
     u.c_first = cluster + 1;
     u.c_last = cluster;
     if (!u.park && b1 < t1) {
@@ -832,8 +844,9 @@ __device__ __forceinline__ void ar_signal_tiles(const ArParams& ar, uint32_t cnt
 template <bool INT8_KIND, bool B_KN, int OUTK, bool SWIGLU, bool AR, bool QA = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : P_THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc, Epi ep, StreamK sk,
-               const __grid_constant__ ArParams ar, const __grid_constant__ QuantA qa, uint32_t* err) {
+               const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+               uint32_t idesc, uint32_t idesc_h, Epi ep, StreamK sk, const __grid_constant__ ArParams ar,
+               const __grid_constant__ QuantA qa, uint32_t* err) {
     static_assert(!AR || OUTK == 1, "the all-reduce signals bf16 tiles");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -877,6 +890,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (sk.half_tiles) tma_prefetch_desc(&tmBh);
         if (OUTK != 2) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
@@ -918,13 +932,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                         qa_part = part;
                     }
                 }
+                // a half tile: this CTA's 64 of the half's 128 columns of B
+                const int hcol = nb * P_BN + (un.half - 1) * 128 + static_cast<int>(rank) * 64;
+                const uint32_t b_bytes = un.half ? P_B_STAGE / 2 : P_B_STAGE;
                 for (int kb = un.kb0; kb < un.kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
-                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_STAGE + P_B_STAGE));
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_STAGE + b_bytes));
                     const uint32_t fb = full_leader + 8u * stage;
                     tma_load_2d_pair(sA + stage * P_A_STAGE, &tmA, fb, kb * BK, mb * P_BM + rank * 128);
-                    if (B_KN) tma_load_2d_pair(sB + stage * P_B_STAGE, &tmB, fb, nb * P_BN + rank * 128, kb * BK);
-                    else tma_load_2d_pair(sB + stage * P_B_STAGE, &tmB, fb, kb * BK, nb * P_BN + rank * 128);
+                    if (un.half) {
+                        if (B_KN) tma_load_2d_pair(sB + stage * P_B_STAGE, &tmBh, fb, hcol, kb * BK);
+                        else tma_load_2d_pair(sB + stage * P_B_STAGE, &tmBh, fb, kb * BK, hcol);
+                    } else if (B_KN) {
+                        tma_load_2d_pair(sB + stage * P_B_STAGE, &tmB, fb, nb * P_BN + rank * 128, kb * BK);
+                    } else {
+                        tma_load_2d_pair(sB + stage * P_B_STAGE, &tmB, fb, kb * BK, nb * P_BN + rank * 128);
+                    }
                     if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
@@ -956,16 +979,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + stage * P_A_STAGE);
                     const uint32_t b_addr = smem_u32(sB + stage * P_B_STAGE);
+                    const uint32_t id = un.half ? idesc_h : idesc;
 #pragma unroll
                     for (int kk = 0; kk < BK / 32; ++kk) {
-                        // per CTA: A is 128 K-major rows; B is 128 columns,
-                        // MN-major (K x N source) or K-major (N x K source)
+                        // per CTA: A is 128 K-major rows; B is 128 columns (64 for a
+                        // half tile), MN-major (K x N source: 128- or 64-byte
+                        // swizzled rows) or K-major (N x K source)
                         const uint64_t adesc = smem_desc_sw128(a_addr + 32u * kk, 16u, 1024u);
-                        const uint64_t bdesc = B_KN ? smem_desc_sw128(b_addr + 4096u * kk, P_B_STAGE, 1024u)
-                                                    : smem_desc_sw128(b_addr + 32u * kk, 16u, 1024u);
+                        uint64_t bdesc;
+                        if (!B_KN) bdesc = smem_desc_sw128(b_addr + 32u * kk, 16u, 1024u);
+                        else if (un.half) bdesc = smem_desc_sw64(b_addr + 2048u * kk, P_B_STAGE, 512u);
+                        else bdesc = smem_desc_sw128(b_addr + 4096u * kk, P_B_STAGE, 1024u);
                         const uint32_t accum = (kb > un.kb0 || kk > 0) ? 1u : 0u;
-                        if (INT8_KIND) mma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
-                        else mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, accum);
+                        if (INT8_KIND) mma_i8_pair(d_tmem, adesc, bdesc, id, accum);
+                        else mma_f8f6f4_pair(d_tmem, adesc, bdesc, id, accum);
                     }
                     tc_commit_pair_mc(&empty[stage], 0x3);
                     if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
@@ -1024,8 +1051,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 }
             }
             const int row = mb * P_BM + row_in_tile;
+            // this warp's columns: 128 of a whole tile, 64 of a half tile
+            const int cw = un.half ? 64 : 128;
+            const int nchunks = cw / 32;
+            const int col_base = nb * P_BN + (un.half ? (un.half - 1) * 128 : 0) + colh * cw;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                   static_cast<uint32_t>(acc * P_BN + colh * 128);
+                                   static_cast<uint32_t>(acc * P_BN + colh * cw);
             if (un.park) {
                 // a later part of a tile another cluster finishes: park the raw accumulators
                 uint4* mine = park_slot(sk.ws, cluster, w16);
@@ -1136,12 +1167,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 for (int q = 0; q < 8; ++q) w[q] = __ldcg(p0 + q * 32 + lane);
             }
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < nchunks; ++c) {
                 tmem_ld_wait();
                 uint32_t cur[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) cur[j] = r[j];
-                if (c + 1 < 4) {
+                if (c + 1 < nchunks) {
                     tmem_ld_32x32b_x32(taddr + 32u * (c + 1), r);  // next chunk in flight
                 } else {
                     // this warp's TMEM columns have all been read: hand them back
@@ -1160,12 +1191,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
 #pragma unroll
                         for (int q = 0; q < 8; ++q) add_parked4<INT8_KIND>(cur, q, __ldcg(pc + q * 32 + lane));
                     }
-                    if (c + 1 < 4) {
+                    if (c + 1 < nchunks) {
 #pragma unroll
                         for (int q = 0; q < 8; ++q) w[q] = __ldcg(p0 + ((c + 1) * 8 + q) * 32 + lane);
                     }
                 }
-                const int col0 = nb * P_BN + colh * 128 + c * 32;
+                const int col0 = col_base + c * 32;
                 if (col0 >= N || row0_warp >= M) continue;
                 if (OUTK == 2) {
                     store_chunk<INT8_KIND>(ep, cur, row, col0, N, rs, row < M);
@@ -1558,7 +1589,8 @@ nq_status_t get_encode_fn(EncodeTiledFn* fn) {
 // 2-D uint8 tensor map: inner extent `inner`, `outer` rows of `ld` bytes,
 // box {box_inner, box_outer}, 128-byte swizzle, zero fill out of bounds.
 nq_status_t make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
-                     uint32_t box_inner, uint32_t box_outer) {
+                     uint32_t box_inner, uint32_t box_outer,
+                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn fn;
     nq_status_t st = get_encode_fn(&fn);
     if (st != NQ_SUCCESS) return st;
@@ -1567,7 +1599,7 @@ nq_status_t make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return NQ_SUCCESS;
@@ -1621,7 +1653,7 @@ nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
 // TMEM accumulator) cost more than the idle half wave saves -- at 4096^3
 // (3.46 waves, 32 k-blocks) whole tiles are 3-5 us faster.
 StreamK plan_stream_k(int tiles, int kblocks, int clusters, bool allowed) {
-    StreamK p{tiles, 0, nullptr, nullptr};
+    StreamK p{tiles, 0, nullptr, nullptr, 0};
     if (!allowed || clusters < 2 || kblocks < 48 || tiles % clusters == 0) return p;
     if (tiles % clusters > clusters / 2) return p;
     const int waves = tiles / clusters;
@@ -1638,11 +1670,15 @@ template <bool I8, bool KN, int OUTK, bool SWIGLU = false, bool AR = false, bool
 nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, void* out, const Epi& ep,
                        cudaStream_t s, const DeviceInfo& di, const ArParams* arp = nullptr,
                        const QuantA* qap = nullptr) {
-    CUtensorMap ma, mb, mc;
+    CUtensorMap ma, mb, mbh, mc;
     nq_status_t st = make_map(&ma, a, d.k, d.m, d.k, BK, 128);
     if (st != NQ_SUCCESS) return st;
     if (KN) st = make_map(&mb, b, d.n, d.k, d.n, 128, BK);
     else st = make_map(&mb, b, d.k, d.n, d.k, BK, 128);
+    if (st != NQ_SUCCESS) return st;
+    // half tiles: 64 columns of B per CTA (K x N: 64-byte swizzled rows)
+    if (KN) st = make_map(&mbh, b, d.n, d.k, d.n, 64, BK, CU_TENSOR_MAP_SWIZZLE_64B);
+    else st = make_map(&mbh, b, d.k, d.n, d.k, BK, 64);
     if (st != NQ_SUCCESS) return st;
     if (d.out_dtype != NQ_S8) {
         nq_gemm_desc_t od = d;
@@ -1653,6 +1689,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     }
     if (st != NQ_SUCCESS) return st;
     const uint32_t idesc = gemm_idesc(d, I8, KN, P_BM, P_BN);
+    const uint32_t idesc_h = gemm_idesc(d, I8, KN, P_BM, P_BN / 2);
     auto kern = k_gemm_tc2<I8, KN, OUTK, SWIGLU, AR, QA>;
     static std::atomic<uint64_t> attr_set{0};
     st = ensure_smem_attr(kern, P_SMEM_BYTES, di.device, &attr_set);
@@ -1675,9 +1712,18 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     const int tiles = ((d.m + P_BM - 1) / P_BM) * ((d.n + P_BN - 1) / P_BN);
     const int kblocks = (d.k + BK - 1) / BK;
     const int resident = std::max(1, max_clusters[di.device & 63].load(std::memory_order_relaxed));
-    const StreamK plan = plan_stream_k(tiles, kblocks, resident, !SWIGLU && !AR);
-    // a QA launch quantizes A on every resident cluster, whatever its tile count
-    const int clusters = (plan.sk_tiles > 0 || QA) ? resident : std::max(1, std::min(tiles, resident));
+    StreamK plan = plan_stream_k(tiles, kblocks, resident, !SWIGLU && !AR);
+    if (!SWIGLU && !AR && plan.sk_tiles == 0) {
+        // a last wave that fills at most half the clusters runs as half tiles
+        const int rem = tiles % resident;
+        if (rem > 0 && 2 * rem <= resident) {
+            plan.dp_tiles = tiles - rem;
+            plan.half_tiles = rem;
+        }
+    }
+    // a QA or half-tile launch uses every resident cluster, whatever its tile count
+    const int clusters = (plan.sk_tiles > 0 || plan.half_tiles > 0 || QA) ? resident
+                                                                         : std::max(1, std::min(tiles, resident));
     constexpr int threads = AR ? P_THREADS_AR : P_THREADS;
     const int grid = 2 * clusters;
     StreamK sk = plan;
@@ -1719,7 +1765,7 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     ArParams ar;
     if (arp) ar = *arp;
     else std::memset(&ar, 0, sizeof(ar));
-    kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mc, d.m, d.n, d.k, idesc, ep, sk, ar, qa, err);
+    kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mbh, mc, d.m, d.n, d.k, idesc, idesc_h, ep, sk, ar, qa, err);
     cudaError_t e = cudaGetLastError();
     if (scratch) scratch_free(scratch, s);
     if (qa_flags) scratch_free(qa_flags, s);

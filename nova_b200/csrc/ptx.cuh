@@ -362,6 +362,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
+// The same descriptor with the 64-byte swizzle (layout type 4): MN-major
+// operands whose tile is 64 bytes wide along MN (8 rows of 64 B per atom).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;
+    d |= 4ull << 61;
+    return d;
+}
+
 // Instruction descriptor of tcgen05.mma kind::f8f6f4 / kind::i8:
 //   [4,6) D format (1 = f32, 2 = s32), [7,10) A format, [10,13) B format,
 //   [15] A major (0 = K), [16] B major (1 = MN), [17,23) N >> 3, [24,29) M >> 4.
