@@ -627,7 +627,6 @@ def tp_parity(mlp, x, y, shards, rows, world, group=None):
     import torch
     import torch.distributed as dist
     import nova_b200.capi as nq
-    from nova_b200.tp import chunk_bounds
     f8 = torch.float8_e4m3fn
     T = x.shape[0]
     idx = torch.tensor(rows, device="cuda")
@@ -668,7 +667,7 @@ def tp_parity(mlp, x, y, shards, rows, world, group=None):
     if world == 1:
         part_err, sum_err = rel(got, part_ref), 0.0
     elif fused is not None:
-        st = fused.state(T, mlp.H, chunk_bounds(T, mlp.chunks))
+        st = fused.state(T, mlp.H, mlp._bounds(T))
         part_gpu = st.partial[idx].double()
         part_err = rel(part_gpu, part_ref)
         total, mag = part_gpu.clone(), part_gpu.abs()

@@ -75,6 +75,55 @@ def chunk_bounds(tokens: int, chunks: int, align: int = 256):
     return [(r0, min(tokens, r0 + step)) for r0 in range(0, tokens, step)]
 
 
+def plan_chunks(tokens: int, n_gate_up: int, k_gate_up: int, n_down: int, k_down: int, tp: int,
+                clusters: int = 74, max_chunks: int = 8, align: int = 256):
+    """Token ranges of the fused TP pipeline (TensorParallelMLP._forward_fused),
+    chosen with a model of it.  Unit of time: the MMAs of one 128-deep
+    k-block of one 256 x 256 tile on one CTA pair (about 0.37 us on a B200).
+      * a GEMM of r row tiles takes ceil(r * ceil(n / 256) / clusters) waves of
+        ceil(k / 128) units: a nearly empty last wave costs a whole wave;
+      * chunk c's all-reduce (its rows x n_down bf16 partial leaving each GPU
+        once, at about 770 GB/s) runs under chunk c+1's GEMMs; the last chunk's
+        is reduced inside its own down GEMM as its tiles complete, so at least
+        one wave's share of it follows that GEMM;
+      * every chunk costs a fixed 25 units of launches and per-token quantize.
+    Candidates: equal splits into 1..max_chunks chunks, and chunks of r row
+    tiles followed by a smaller remainder.  The cheapest plan wins (fewer
+    chunks on ties).  tp == 1 has no all-reduce: one chunk."""
+    if tokens <= 0:
+        return []
+    if tp <= 1:
+        return [(0, tokens)]
+    unit_s = 0.37e-6
+    link_bytes_per_unit = 770e9 * unit_s
+    nt_gu, nt_dn = -(-n_gate_up // 256), -(-n_down // 256)
+    kb_gu, kb_dn = -(-k_gate_up // 128), -(-k_down // 128)
+
+    def cost(bounds):
+        t = ar_free = 0.0
+        for c, (r0, r1) in enumerate(bounds):
+            r = -(-(r1 - r0) // align)
+            t += 25.0 + -(-(r * nt_gu) // clusters) * kb_gu
+            dn_start = t
+            waves_dn = -(-(r * nt_dn) // clusters)
+            t += waves_dn * kb_dn
+            ar = (r1 - r0) * n_down * 2 / link_bytes_per_unit
+            if c < len(bounds) - 1:
+                ar_free = max(ar_free, t) + ar
+            else:
+                ar_free = max(max(ar_free, dn_start) + ar, t + ar / waves_dn)
+        return max(t, ar_free)
+
+    cands = [chunk_bounds(tokens, c, align) for c in range(1, max_chunks + 1)]
+    for r in range(1, -(-tokens // align) + 1):
+        step = r * align
+        b = [(r0, min(tokens, r0 + step)) for r0 in range(0, tokens, step)]
+        if len(b) <= max_chunks:
+            cands.append(b)
+    best = min(cands, key=lambda b: (round(cost(b), 6), len(b)))
+    return best
+
+
 def reduce_pipeline(bounds, compute, group=None, tp: int = 1):
     """For each token range: compute(r0, r1) enqueues the partial rows and
     returns the tensor view holding them; with tp > 1 an asynchronous sum
@@ -386,7 +435,7 @@ class TensorParallelMLP:
     GEMM with the SwiGLU epilogue produces silu(g) * u directly."""
 
     def __init__(self, hidden_dim: int, intermediate_size: int, group=None, chunks=None,
-                 overlap: str = "full", allreduce: str = "auto"):
+                 overlap: str = "full", allreduce: str = "auto", chunk_rows=None):
         import torch
         if overlap not in ("full", "down"):
             raise ValueError("overlap must be 'full' or 'down'")
@@ -405,9 +454,24 @@ class TensorParallelMLP:
         # c+1's gate/up GEMM (measured at tp = 8: 1.75 ms with 1 chunk, 1.56
         # with 2 or 4, 1.78 with 8, T = 16384, H = 8192, I = 28672)
         self.chunks = chunks if chunks is not None else (1 if self.tp <= 2 else 4)
+        # chunk_rows: tokens per chunk (a multiple of 256; the last chunk takes
+        # the remainder) instead of `chunks` equal chunks; "plan": plan_chunks'
+        # model of the pipeline
+        if chunk_rows is not None and chunk_rows != "plan" and (int(chunk_rows) <= 0 or int(chunk_rows) % 256):
+            raise ValueError("chunk_rows must be a positive multiple of 256 or 'plan'")
+        self.chunk_rows = chunk_rows
         self.gate_up = _FP8Linear()
         self.down = RowParallelLayer(intermediate_size, hidden_dim, group, self.chunks, allreduce)
         self._h = {}
+
+    def _bounds(self, T):
+        """Token ranges of the chunked pipeline for T tokens."""
+        if self.chunk_rows == "plan":
+            return plan_chunks(T, 2 * self.I_local, self.H, self.H, self.I_local, self.tp)
+        if self.chunk_rows:
+            step = int(self.chunk_rows)
+            return [(r0, min(T, r0 + step)) for r0 in range(0, T, step)]
+        return chunk_bounds(T, self.chunks)
 
     def set_weight(self, gate_weight, up_weight, down_weight):
         """Full weights (host or device, fp32): keeps this rank's shards."""
@@ -443,7 +507,7 @@ class TensorParallelMLP:
         xq, sx = self.gate_up.act(input, T)
         if self.down.fused is not None:
             return self._forward_fused(xq, sx, h, output, T, sync)
-        bounds = chunk_bounds(T, self.chunks)
+        bounds = self._bounds(T)
         if self.overlap == "down" or len(bounds) == 1:
             self.gate_up.gemm(xq, sx, h, 0, T, epilogue=epi)
 
@@ -467,7 +531,7 @@ class TensorParallelMLP:
         t, nq = self.torch, self.gate_up.nq
         s = t.cuda.current_stream().cuda_stream
         ar, down, gu = self.down.fused, self.down.lin, self.gate_up
-        bounds = chunk_bounds(T, self.chunks)
+        bounds = self._bounds(T)
         st = ar.state(T, self.H, bounds)
         ar.begin(st)
         C = len(bounds)

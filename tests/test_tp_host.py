@@ -47,6 +47,30 @@ def test_chunk_bounds_cover_tokens(tokens, chunks):
     assert tp.chunk_bounds(0, 4) == []
 
 
+@pytest.mark.parametrize("tokens,tp_", [(16384, 8), (16384, 4), (16384, 2), (300, 8), (1, 4), (4097, 8), (16384, 1)])
+def test_plan_chunks_cover_tokens(tokens, tp_):
+    b = tp.plan_chunks(tokens, 2 * 28672 // tp_, 8192, 8192, 28672 // tp_, tp_)
+    assert b[0][0] == 0 and b[-1][1] == tokens
+    assert all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+    assert all((r0 % 256) == 0 and r1 > r0 for r0, r1 in b)
+    assert 1 <= len(b) <= 8
+    if tp_ == 1:
+        assert b == [(0, tokens)]
+    assert tp.plan_chunks(0, 256, 256, 256, 256, 4) == []
+
+
+def test_mlp_chunk_rows_option():
+    mlp = tp.TensorParallelMLP(256, 512, chunk_rows=512)
+    assert mlp._bounds(1300) == [(0, 512), (512, 1024), (1024, 1300)]
+    mlp = tp.TensorParallelMLP(256, 512, chunks=3)
+    assert mlp._bounds(1300) == tp.chunk_bounds(1300, 3)
+    mlp = tp.TensorParallelMLP(256, 512, chunk_rows="plan")
+    assert mlp._bounds(1300) == [(0, 1300)]      # tp = 1: one chunk
+    for bad in (0, -256, 300, "many"):
+        with pytest.raises(ValueError):
+            tp.TensorParallelMLP(256, 512, chunk_rows=bad)
+
+
 def test_packed_swiglu_equals_separate_gate_up():
     """The packed GEMM's accumulators are the separate gate/up accumulators
     permuted (bit-identical), and the SwiGLU epilogue on them equals
