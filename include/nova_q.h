@@ -64,7 +64,9 @@ const char* nq_status_string(nq_status_t s);
 const char* nq_last_error(void);
 int nq_version(void);
 /* Reads (and with clear != 0 resets) the device-side error word of the
-   current device: bit 0 = a bounded wait in a kernel timed out. */
+   current device: bit 0 = a bounded wait in a kernel timed out.  Clearing also
+   resets the library's per-stream completion flags of that device, which a
+   wait that ran out may have left raised. */
 nq_status_t nq_device_error_flags(uint32_t* flags, int clear);
 /* Upper bound, in ns, of a kernel's wait on counts sent by other GPUs (the
    fused all-reduce below; default 5 s, 0 restores the default).  Applies to

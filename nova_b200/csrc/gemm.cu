@@ -1312,7 +1312,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
 template <int BT>
 struct DecodeCfg {
     static constexpr int B_STAGE = BT * BK;
-    // as many stages as fit (up to 8: ~128 KB of weights in flight per SM)
+    // as many stages as fit (up to 8: ~128 KB of weights in flight per SM;
+    // measured on B200: 12 stages, or L2 prefetches further ahead, stream no faster)
     static constexpr int STAGES = (200 * 1024) / (A_STAGE + B_STAGE) < 8 ? (200 * 1024) / (A_STAGE + B_STAGE) : 8;
     static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
     static constexpr uint32_t TMEM = BT <= 16 ? 32 : (BT <= 32 ? 64 : (BT <= 64 ? 128 : (BT <= 128 ? 256 : 512)));
@@ -1425,6 +1426,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else {
         const int quarter = warp & 3;
         const int nl = quarter * 32 + lane;  // weight row within the slice
+        // up to 32 tokens: the row scales and the later CTAs' parked parts sit
+        // in registers, so the last segment's epilogue (the kernel's tail)
+        // waits on no memory after its accumulator is ready
+        constexpr bool PRE = BT <= 32;
+        float rsv[PRE ? BT : 1];
+        if constexpr (PRE) {
+#pragma unroll
+            for (int t = 0; t < BT; ++t) rsv[t] = (ep.row_scale && t < M) ? __ldg(ep.row_scale + t) : 1.0f;
+        }
+        const int odt = ep.out_dtype;
         int seg = 0;
         for (long long s0 = b0; s0 < b1; ++seg) {
             const int slice = static_cast<int>(s0 / kblocks);
@@ -1432,13 +1443,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const long long s1 = min(b1, slice_end);
             const bool head = (s0 % kblocks) == 0;  // this CTA holds the slice's first k-block
             const int acc = seg & 1;
-            bool ok = mbar_wait(&tfull[acc], (static_cast<uint32_t>(seg) >> 1) & 1u, err);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            tc_fence_after();
+            const uint32_t tpar = (static_cast<uint32_t>(seg) >> 1) & 1u;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BT);
-            uint32_t* mine = ws + static_cast<size_t>(blockIdx.x) * BT * 128;
             if (!head) {
                 // a later part of a slice owned by an earlier CTA: park it
+                uint32_t* mine = ws + static_cast<size_t>(blockIdx.x) * BT * 128;
+                bool ok = mbar_wait(&tfull[acc], tpar, err);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < BT; c += 16) {
                     uint32_t r[16];
@@ -1451,7 +1463,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 mbar_arrive(&tempty[acc]);
                 __threadfence();
                 __syncwarp();
-                if (lane == 0) atomicAdd(flags + blockIdx.x, 1u);
+                // one flag per (CTA, epilogue warp): the owner's warp of the same
+                // quarter reads exactly these 32 rows
+                if (lane == 0) atomicAdd(flags + blockIdx.x * 4 + quarter, 1u);
                 s0 = s1;
                 continue;
             }
@@ -1461,45 +1475,91 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 c_last = c_first;
                 while (c_last + 1 < G && range_begin(total, c_last + 1, G) < slice_end) ++c_last;
                 if (lane == 0)
-                    for (int c = c_first; c <= c_last; ++c) wait_flag_geq(flags + c, 4u, err);
+                    for (int c = c_first; c <= c_last; ++c) wait_flag_geq(flags + c * 4 + quarter, 1u, err);
                 __syncwarp();
             }
             const int n = slice * 128 + nl;
             const float cs = ep.col_scale && n < N ? __ldg(ep.col_scale + n) : 1.0f;
             const float bs = ep.bias && n < N ? __ldg(ep.bias + n) : -0.0f;
-#pragma unroll 1
-            for (int c = 0; c < BT; c += 16) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(taddr + c, r);
-                tmem_ld_wait();
+            // the later parts' sum (int32 exact; fp32 in CTA order), read while
+            // this CTA's own MMAs of the slice are still running
+            uint32_t pre[PRE ? BT : 1];
+            if constexpr (PRE) {
+#pragma unroll
+                for (int j = 0; j < BT; ++j) pre[j] = 0u;
                 for (int cc = c_first; cc <= c_last; ++cc) {
                     const uint32_t* part = ws + static_cast<size_t>(cc) * BT * 128;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const uint32_t q = __ldcg(part + (c + j) * 128 + nl);
-                        if (INT8_KIND) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + static_cast<int32_t>(q));
-                        else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(q)));
-                    }
-                }
-                if (n < N) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = c + j;
-                        if (t >= M) break;
-                        const size_t o = static_cast<size_t>(t) * ep.ldo + n;
-                        if (INT8_KIND && ep.out_dtype == NQ_S32) {
-                            static_cast<int32_t*>(ep.out)[o] = static_cast<int32_t>(r[j]);
-                            continue;
-                        }
-                        const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
-                        const float rs = ep.row_scale ? __ldg(ep.row_scale + t) : 1.0f;
-                        const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(a, ep.alpha), rs), cs), bs);
-                        if (ep.out_dtype == NQ_BF16) static_cast<uint16_t*>(ep.out)[o] = static_cast<uint16_t>(f32x2_to_bf16x2(v, 0.0f));
-                        else if (ep.out_dtype == NQ_S8) static_cast<int8_t*>(ep.out)[o] = requant_s8(v);
-                        else static_cast<float*>(ep.out)[o] = v;
+                    for (int j = 0; j < BT; ++j) {
+                        const uint32_t q = __ldcg(part + j * 128 + nl);
+                        if (INT8_KIND) pre[j] = static_cast<uint32_t>(static_cast<int32_t>(pre[j]) + static_cast<int32_t>(q));
+                        else pre[j] = cc == c_first ? q : __float_as_uint(__fadd_rn(__uint_as_float(pre[j]), __uint_as_float(q)));
                     }
                 }
             }
+            bool ok = mbar_wait(&tfull[acc], tpar, err);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            auto emit = [&](int c, uint32_t (&r)[16]) {
+                if (n >= N) return;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = c + j;
+                    if (t < M) {
+                        const size_t o = static_cast<size_t>(t) * ep.ldo + n;
+                        if (INT8_KIND && odt == NQ_S32) {
+                            static_cast<int32_t*>(ep.out)[o] = static_cast<int32_t>(r[j]);
+                        } else {
+                            const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+                            float rs;
+                            if constexpr (PRE) rs = rsv[t];
+                            else rs = ep.row_scale ? __ldg(ep.row_scale + t) : 1.0f;
+                            const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(a, ep.alpha), rs), cs), bs);
+                            if (odt == NQ_BF16) static_cast<uint16_t*>(ep.out)[o] = static_cast<uint16_t>(f32x2_to_bf16x2(v, 0.0f));
+                            else if (odt == NQ_S8) static_cast<int8_t*>(ep.out)[o] = requant_s8(v);
+                            else static_cast<float*>(ep.out)[o] = v;
+                        }
+                    }
+                }
+            };
+            if constexpr (PRE) {
+                const bool split = c_last >= c_first;
+#pragma unroll
+                for (int c = 0; c < BT; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(taddr + c, r);
+                    tmem_ld_wait();
+                    if (split) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if (INT8_KIND) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + static_cast<int32_t>(pre[c + j]));
+                            else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(pre[c + j])));
+                        }
+                    }
+                    emit(c, r);
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BT; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(taddr + c, r);
+                    tmem_ld_wait();
+                    for (int cc = c_first; cc <= c_last; ++cc) {
+                        const uint32_t* part = ws + static_cast<size_t>(cc) * BT * 128;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const uint32_t q = __ldcg(part + (c + j) * 128 + nl);
+                            if (INT8_KIND) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + static_cast<int32_t>(q));
+                            else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(q)));
+                        }
+                    }
+                    emit(c, r);
+                }
+            }
+            // each parked part has exactly one reader (a CTA parks at most the
+            // first segment of its range): clear its flags for the next launch
+            if (lane == 0)
+                for (int cc = c_first; cc <= c_last; ++cc) flags[cc * 4 + quarter] = 0u;
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             s0 = s1;
@@ -1791,14 +1851,23 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
     if (st != NQ_SUCCESS) return st;
     const long long total = static_cast<long long>((d.n + 127) / 128) * ((d.k + BK - 1) / BK);
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(total, di.sm_count)));
-    // per CTA one parked partial (BT x 128 accumulators) and one flag
+    // per CTA one parked partial (BT x 128 accumulators) and four flags (one per
+    // epilogue warp), taken from the stream's flag words, which every launch
+    // leaves cleared: no memset on the launch path
     const size_t ws_bytes = static_cast<size_t>(grid) * BT * 128 * 4;
-    const size_t fl_bytes = static_cast<size_t>(grid) * 4;
-    void* ws = nullptr;
-    st = scratch_alloc(&ws, ws_bytes + fl_bytes, s);
+    const size_t fl_bytes = static_cast<size_t>(grid) * 4 * 4;
+    uint32_t* flags = nullptr;
+    st = stream_flags(&flags, grid * 4, s);
     if (st != NQ_SUCCESS) return st;
-    uint32_t* flags = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ws_bytes);
-    cudaError_t e = cudaMemsetAsync(flags, 0, fl_bytes, s);
+    void* ws = nullptr;
+    st = scratch_alloc(&ws, ws_bytes + (flags ? 0 : fl_bytes), s);
+    if (st != NQ_SUCCESS) return st;
+    cudaError_t e = cudaSuccess;
+    if (!flags) {
+        // inside a graph capture: flags of this launch, cleared by a memset node
+        flags = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ws_bytes);
+        e = cudaMemsetAsync(flags, 0, fl_bytes, s);
+    }
     if (e == cudaSuccess) {
         kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(mw, mx, d.m, d.n, d.k, idesc, ep, static_cast<uint32_t*>(ws), flags,
                                                     device_error_word());

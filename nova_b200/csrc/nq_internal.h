@@ -33,6 +33,16 @@ nq_status_t current_device(DeviceInfo* out);
 nq_status_t scratch_alloc(void** p, size_t bytes, cudaStream_t s);
 void scratch_free(void* p, cudaStream_t s);
 
+// Zero-initialised flag words owned by (current device, stream), at least
+// `count` of them, for kernels that clear every flag they raise before they
+// finish (so the next launch on the stream finds them zero without a memset).
+// While the stream is capturing a graph *p is nullptr: the caller then takes
+// flags from its scratch and clears them inside the graph.
+nq_status_t stream_flags(uint32_t** p, int count, cudaStream_t s);
+// Clears every stream's flags of the current device (after a bounded wait has
+// given up, a flag may have been left raised).  The device must be idle.
+nq_status_t clear_stream_flags();
+
 // Device address of the error word of the current device (kernels OR their
 // error bits into it), or nullptr if it cannot be resolved.
 uint32_t* device_error_word();

@@ -3,6 +3,7 @@
 #include <atomic>
 #include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "nq_internal.h"
 #include "ptx.cuh"
@@ -98,6 +99,58 @@ void scratch_free(void* p, cudaStream_t s) {
     if (p) cudaFreeAsync(p, s);
 }
 
+namespace {
+constexpr int kStreamFlagWords = 4096;
+struct StreamFlags {
+    int device;
+    cudaStream_t stream;
+    uint32_t* words;
+};
+std::mutex g_flags_mu;
+std::vector<StreamFlags> g_flags;  // kept for the life of the process (16 KB per stream used)
+}  // namespace
+
+nq_status_t stream_flags(uint32_t** p, int count, cudaStream_t s) {
+    *p = nullptr;
+    if (count > kStreamFlagWords) return fail(NQ_ERROR_INVALID_VALUE, "stream flags: too many words requested");
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    NQ_CHECK_CUDA(cudaStreamIsCapturing(s, &cs), "cudaStreamIsCapturing");
+    if (cs != cudaStreamCaptureStatusNone) return NQ_SUCCESS;
+    int dev = -1;
+    NQ_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_flags_mu);
+    for (const auto& f : g_flags)
+        if (f.device == dev && f.stream == s) {
+            *p = f.words;
+            return NQ_SUCCESS;
+        }
+    uint32_t* w = nullptr;
+    if (cudaMalloc(&w, kStreamFlagWords * sizeof(uint32_t)) != cudaSuccess) {
+        // e.g. another thread is capturing a graph in global mode: the caller
+        // takes per-launch flags this time
+        (void)cudaGetLastError();
+        return NQ_SUCCESS;
+    }
+    cudaError_t e = cudaMemsetAsync(w, 0, kStreamFlagWords * sizeof(uint32_t), s);
+    if (e != cudaSuccess) {
+        cudaFree(w);
+        return cuda_status(e, "cudaMemsetAsync(stream flags)");
+    }
+    g_flags.push_back({dev, s, w});
+    *p = w;
+    return NQ_SUCCESS;
+}
+
+nq_status_t clear_stream_flags() {
+    int dev = -1;
+    NQ_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_flags_mu);
+    for (const auto& f : g_flags)
+        if (f.device == dev)
+            NQ_CHECK_CUDA(cudaMemset(f.words, 0, kStreamFlagWords * sizeof(uint32_t)), "cudaMemset(stream flags)");
+    return NQ_SUCCESS;
+}
+
 uint32_t* device_error_word() {
     // Host code cannot name a __device__ variable's address directly: the
     // symbol's address is looked up once per device with that device current.
@@ -156,6 +209,9 @@ nq_status_t nq_device_error_flags(uint32_t* flags, int clear) {
         uint32_t z = 0;
         NQ_CHECK_CUDA(cudaMemcpyToSymbol(nq_device_error_word, &z, sizeof(uint32_t)),
                       "nq_device_error_flags: clear");
+        st = nq::clear_stream_flags();
+        if (st != NQ_SUCCESS) return st;
+        NQ_CHECK_CUDA(cudaDeviceSynchronize(), "nq_device_error_flags: clear flags");
     }
     return NQ_SUCCESS;
 }

@@ -316,6 +316,66 @@ def test_decode_config3_full_size_vs_torch(nq):
     assert nq.device_error_flags() == 0
 
 
+def test_decode_flags_across_launches_streams_and_graphs(nq):
+    """The decode path's stream-K fixup flags live in a per-stream buffer that
+    each launch leaves cleared (no memset per launch), and in a memset node of
+    their own inside a graph capture: launches of different shapes back to back
+    on one stream, on two streams at once, and a captured graph replayed three
+    times must all stay exact against torch._int_mm."""
+    import torch
+    k, n = 8192, 28672
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+    wt = w.t().contiguous()
+    cases = {}
+    for m in (16, 32, 7):
+        x = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+        xm = torch.zeros(32, k, dtype=torch.int8, device="cuda")
+        xm[:m] = x
+        cases[m] = (x, torch._int_mm(xm, wt)[:m])
+    outs = {m: torch.empty(m, n, dtype=torch.int32, device="cuda") for m in cases}
+
+    def launch(m, stream):
+        x, _ = cases[m]
+        nq.gemm(nq.make_desc(m, n, k, 2, 2, 1, 2, 1.0), x.data_ptr(), w.data_ptr(), outs[m].data_ptr(),
+                stream.cuda_stream)
+
+    def check():
+        for m, (_, ref) in cases.items():
+            assert torch.equal(outs[m], ref), m
+            outs[m].fill_(0)
+
+    s0 = torch.cuda.current_stream()
+    for _ in range(3):
+        for m in (16, 32, 7, 16):
+            launch(m, s0)
+    torch.cuda.synchronize()
+    check()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    s1.wait_stream(s0)
+    s2.wait_stream(s0)
+    for _ in range(4):
+        launch(16, s1)
+        launch(32, s2)
+    launch(7, s1)
+    torch.cuda.synchronize()
+    check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cs = torch.cuda.current_stream()
+        for m in (16, 32, 7):
+            launch(m, cs)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        check()
+    del graph
+    launch(16, s0)                      # the stream's own flags are still clear
+    torch.cuda.synchronize()
+    assert torch.equal(outs[16], cases[16][1])
+    assert nq.device_error_flags() == 0
+
+
 def run_swiglu(nq, a, b, m, n, k, b_layout, out_dtype, alpha, row=None, col=None, bias=None):
     from gpu_util import dev, empty, host, ptr, stream
     d_a, d_b = dev(a), dev(b)
