@@ -1298,7 +1298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
 }
 
 // ---------------- decode-shaped kernel (few tokens, many output channels) ----------------
-// For M <= 256 tokens against a large weight the roles are swapped: 128 weight
+// For M <= 64 tokens against a large weight the roles are swapped: 128 weight
 // rows form the MMA's M side and the (padded) tokens its N side
 // (tcgen05.mma M=128, N=BT), so one MMA tile covers all tokens.  The work --
 // weight slices of 128 rows times k-blocks, in slice-major order -- is cut into
@@ -1309,35 +1309,64 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
 // its raw accumulators in its own workspace row and raises its flag, and the
 // owner adds them in CTA order before the epilogue -- no atomics, exact for
 // int32 and deterministic for fp32.
+//
+// Stores leave through the TMA: while every SM streams weights at full rate,
+// thread-level global loads and stores wait microseconds each (a 64-token
+// slice written row by row took ~10 us on B200, longer than the weights it
+// streamed).  So the epilogue warps write a slice's outputs (or a parked part)
+// into shared memory and one thread sends it with one bulk store, and the
+// producer warp, once its last weight load is issued, fetches the later CTA's
+// parked part of this CTA's last slice with one bulk load.
 template <int BT>
 struct DecodeCfg {
     static constexpr int B_STAGE = BT * BK;
-    // as many stages as fit (up to 8: ~128 KB of weights in flight per SM;
-    // measured on B200: 12 stages, or L2 prefetches further ahead, stream no faster)
-    static constexpr int STAGES = (200 * 1024) / (A_STAGE + B_STAGE) < 8 ? (200 * 1024) / (A_STAGE + B_STAGE) : 8;
-    static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
-    static constexpr uint32_t TMEM = BT <= 16 ? 32 : (BT <= 32 ? 64 : (BT <= 64 ? 128 : (BT <= 128 ? 256 : 512)));
+    static constexpr int OUT_BYTES = BT * 128 * 4;  // a slice of outputs (any type) or of raw accumulators
+    // as many stages as fit beside the two epilogue buffers (up to 8: ~128 KB of
+    // weights in flight per SM; measured on B200: 12 stages, or L2 prefetches
+    // further ahead, stream no faster)
+    static constexpr int BUDGET = 216 * 1024 - 2 * OUT_BYTES;
+    static constexpr int STAGES = BUDGET / (A_STAGE + B_STAGE) < 8 ? BUDGET / (A_STAGE + B_STAGE) : 8;
+    static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_STAGE) + 2 * OUT_BYTES + BT * 4 + 256;
+    static constexpr uint32_t TMEM = BT <= 16 ? 32 : (BT <= 32 ? 64 : 128);
 };
 
 __device__ __forceinline__ long long range_begin(long long total, int c, int G) { return total * c / G; }
 
+// Later CTAs whose ranges touch the slice that starts at k-block s0 and is cut
+// at this CTA's range end b1 (c_first > c_last when none).
+__device__ __forceinline__ void decode_later_ctas(long long total, int G, long long s1, long long slice_end, int* c_first,
+                                                  int* c_last) {
+    *c_first = blockIdx.x + 1;
+    *c_last = blockIdx.x;
+    if (s1 < slice_end) {
+        int c = blockIdx.x + 1;
+        while (c + 1 < G && range_begin(total, c + 1, G) < slice_end) ++c;
+        *c_last = c;
+    }
+}
+
 template <bool INT8_KIND, bool W_KN, int BT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm_decode(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
-                  uint32_t idesc, Epi ep, uint32_t* ws, uint32_t* flags, uint32_t* err) {
+    k_gemm_decode(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                  const __grid_constant__ CUtensorMap tmO, int tma_out, int M, int N, int K, uint32_t idesc, Epi ep,
+                  uint32_t* ws, uint32_t* flags, uint32_t* err) {
     using Cfg = DecodeCfg<BT>;
     constexpr int D_STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
     uint8_t* sX = smem + D_STAGES * A_STAGE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sX + D_STAGES * Cfg::B_STAGE);
+    uint8_t* sOut = sX + D_STAGES * Cfg::B_STAGE;            // outputs or a part to park
+    uint32_t* sPart = reinterpret_cast<uint32_t*>(sOut + Cfg::OUT_BYTES);  // a later CTA's parked part
+    float* sRs = reinterpret_cast<float*>(sOut + 2 * Cfg::OUT_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRs + BT + ((BT & 1) ? 1 : 0));
     uint64_t* full = bars;
     uint64_t* empty = bars + D_STAGES;
     uint64_t* tfull = bars + 2 * D_STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* done = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* pfull = done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pfull + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1346,6 +1375,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const long long total = static_cast<long long>((N + 127) / 128) * kblocks;
     const long long b0 = range_begin(total, blockIdx.x, G);
     const long long b1 = range_begin(total, blockIdx.x + 1, G);
+    // this CTA's last segment: does it own a slice that later CTAs finish?
+    const int last_slice = static_cast<int>((b1 - 1) / kblocks);
+    const long long last_s0 = max(b0, static_cast<long long>(last_slice) * kblocks);
+    int lc_first, lc_last;
+    decode_later_ctas(total, G, b1, static_cast<long long>(last_slice + 1) * kblocks, &lc_first, &lc_last);
+    const bool last_fetch = (last_s0 % kblocks) == 0 && lc_last == lc_first;  // one later part: bulk-fetched
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < D_STAGES; ++s) {
@@ -1357,15 +1392,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(&tempty[a], 128);
         }
         mbar_init(done, 1);
+        mbar_init(pfull, 1);
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
+        if (tma_out) tma_prefetch_desc(&tmO);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, Cfg::TMEM);
         tmem_relinquish();
+    }
+    if (threadIdx.x >= 64 && threadIdx.x < 64 + BT) {
+        const int t = threadIdx.x - 64;
+        sRs[t] = (ep.row_scale && t < M) ? __ldg(ep.row_scale + t) : 1.0f;
     }
     tc_fence_before();
     __syncthreads();
@@ -1384,6 +1425,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 else tma_load_2d(sW + stage * A_STAGE, &tmW, &full[stage], kb * BK, slice * 128);
                 tma_load_2d(sX + stage * Cfg::B_STAGE, &tmX, &full[stage], kb * BK, 0);
                 if (++stage == D_STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (last_fetch) {
+                // the later CTA parked its part long ago (it was the start of its range)
+                if (wait_flag_geq(flags + lc_first * 4, 1u, err)) {
+                    fence_proxy_async_global();
+                    mbar_arrive_expect_tx(pfull, Cfg::OUT_BYTES);
+                    bulk_load_1d(sPart, ws + static_cast<size_t>(lc_first) * BT * 128, Cfg::OUT_BYTES, pfull);
+                } else {
+                    mbar_arrive(pfull);
+                }
             }
         }
     } else if (warp == 1) {
@@ -1426,16 +1477,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else {
         const int quarter = warp & 3;
         const int nl = quarter * 32 + lane;  // weight row within the slice
-        // up to 32 tokens: the row scales and the later CTAs' parked parts sit
-        // in registers, so the last segment's epilogue (the kernel's tail)
-        // waits on no memory after its accumulator is ready
-        constexpr bool PRE = BT <= 32;
-        float rsv[PRE ? BT : 1];
-        if constexpr (PRE) {
-#pragma unroll
-            for (int t = 0; t < BT; ++t) rsv[t] = (ep.row_scale && t < M) ? __ldg(ep.row_scale + t) : 1.0f;
-        }
+        const bool issuer = threadIdx.x == 64;
         const int odt = ep.out_dtype;
+        const int esize = odt == NQ_BF16 ? 2 : (odt == NQ_S8 ? 1 : 4);
+        // After a wait that ran out (error bit set) the warps still pass every
+        // named barrier in the same order, with garbage data: none may leave
+        // the protocol early while the others wait at a barrier.
+        bool failed = false;
         int seg = 0;
         for (long long s0 = b0; s0 < b1; ++seg) {
             const int slice = static_cast<int>(s0 / kblocks);
@@ -1445,105 +1493,68 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int acc = seg & 1;
             const uint32_t tpar = (static_cast<uint32_t>(seg) >> 1) & 1u;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BT);
+            uint32_t* sOut32 = reinterpret_cast<uint32_t*>(sOut);
             if (!head) {
-                // a later part of a slice owned by an earlier CTA: park it
-                uint32_t* mine = ws + static_cast<size_t>(blockIdx.x) * BT * 128;
-                bool ok = mbar_wait(&tfull[acc], tpar, err);
-                if (!__all_sync(0xffffffffu, ok)) break;
+                // a later part of a slice owned by an earlier CTA: park it with one
+                // bulk store of [token][row] accumulators, then raise the flag
+                if (!failed && !__all_sync(0xffffffffu, mbar_wait(&tfull[acc], tpar, err))) failed = true;
                 tc_fence_after();
+                named_bar_sync(1, 128);  // the previous bulk store has read sOut
 #pragma unroll 1
                 for (int c = 0; c < BT; c += 16) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(taddr + c, r);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) __stcg(mine + (c + j) * 128 + nl, r[j]);
+                    for (int j = 0; j < 16; ++j) sOut32[(c + j) * 128 + nl] = r[j];
                 }
                 tc_fence_before();
                 mbar_arrive(&tempty[acc]);
-                __threadfence();
-                __syncwarp();
-                // one flag per (CTA, epilogue warp): the owner's warp of the same
-                // quarter reads exactly these 32 rows
-                if (lane == 0) atomicAdd(flags + blockIdx.x * 4 + quarter, 1u);
+                fence_proxy_async_smem();
+                named_bar_sync(1, 128);
+                if (issuer) {
+                    bulk_store_1d(ws + static_cast<size_t>(blockIdx.x) * BT * 128, sOut, Cfg::OUT_BYTES);
+                    bulk_commit_group();
+                    bulk_wait_group<0>();  // the part is in global memory
+                    fence_proxy_async_global();
+                    __threadfence();
+                    atomicAdd(flags + blockIdx.x * 4, 1u);
+                }
                 s0 = s1;
                 continue;
             }
             // owner: later CTAs touching this slice (if the range ends inside it)
-            int c_first = blockIdx.x + 1, c_last = blockIdx.x;
-            if (s1 < slice_end) {
-                c_last = c_first;
-                while (c_last + 1 < G && range_begin(total, c_last + 1, G) < slice_end) ++c_last;
+            int c_first, c_last;
+            decode_later_ctas(total, G, s1, slice_end, &c_first, &c_last);
+            const bool split = c_last >= c_first;
+            const bool fetched = split && s1 == b1 && last_fetch;  // the producer bulk-loads the part
+            if (split && !fetched) {
                 if (lane == 0)
-                    for (int c = c_first; c <= c_last; ++c) wait_flag_geq(flags + c * 4 + quarter, 1u, err);
+                    for (int c = c_first; c <= c_last; ++c) wait_flag_geq(flags + c * 4, 1u, err);
                 __syncwarp();
             }
             const int n = slice * 128 + nl;
             const float cs = ep.col_scale && n < N ? __ldg(ep.col_scale + n) : 1.0f;
             const float bs = ep.bias && n < N ? __ldg(ep.bias + n) : -0.0f;
-            // the later parts' sum (int32 exact; fp32 in CTA order), read while
-            // this CTA's own MMAs of the slice are still running
-            uint32_t pre[PRE ? BT : 1];
-            if constexpr (PRE) {
-#pragma unroll
-                for (int j = 0; j < BT; ++j) pre[j] = 0u;
-                for (int cc = c_first; cc <= c_last; ++cc) {
-                    const uint32_t* part = ws + static_cast<size_t>(cc) * BT * 128;
-#pragma unroll
-                    for (int j = 0; j < BT; ++j) {
-                        const uint32_t q = __ldcg(part + j * 128 + nl);
-                        if (INT8_KIND) pre[j] = static_cast<uint32_t>(static_cast<int32_t>(pre[j]) + static_cast<int32_t>(q));
-                        else pre[j] = cc == c_first ? q : __float_as_uint(__fadd_rn(__uint_as_float(pre[j]), __uint_as_float(q)));
-                    }
-                }
-            }
-            bool ok = mbar_wait(&tfull[acc], tpar, err);
-            if (!__all_sync(0xffffffffu, ok)) break;
+            if (fetched && !failed && !__all_sync(0xffffffffu, mbar_wait(pfull, 0, err))) failed = true;
+            if (!failed && !__all_sync(0xffffffffu, mbar_wait(&tfull[acc], tpar, err))) failed = true;
             tc_fence_after();
-            auto emit = [&](int c, uint32_t (&r)[16]) {
-                if (n >= N) return;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = c + j;
-                    if (t < M) {
-                        const size_t o = static_cast<size_t>(t) * ep.ldo + n;
-                        if (INT8_KIND && odt == NQ_S32) {
-                            static_cast<int32_t*>(ep.out)[o] = static_cast<int32_t>(r[j]);
-                        } else {
-                            const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
-                            float rs;
-                            if constexpr (PRE) rs = rsv[t];
-                            else rs = ep.row_scale ? __ldg(ep.row_scale + t) : 1.0f;
-                            const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(a, ep.alpha), rs), cs), bs);
-                            if (odt == NQ_BF16) static_cast<uint16_t*>(ep.out)[o] = static_cast<uint16_t>(f32x2_to_bf16x2(v, 0.0f));
-                            else if (odt == NQ_S8) static_cast<int8_t*>(ep.out)[o] = requant_s8(v);
-                            else static_cast<float*>(ep.out)[o] = v;
-                        }
-                    }
-                }
-            };
-            if constexpr (PRE) {
-                const bool split = c_last >= c_first;
-#pragma unroll
-                for (int c = 0; c < BT; c += 16) {
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(taddr + c, r);
-                    tmem_ld_wait();
-                    if (split) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            if (INT8_KIND) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + static_cast<int32_t>(pre[c + j]));
-                            else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(pre[c + j])));
-                        }
-                    }
-                    emit(c, r);
-                }
-            } else {
+            // the previous bulk store has read sOut, and every warp has passed its
+            // flag wait (so the flags can be cleared below)
+            named_bar_sync(1, 128);
 #pragma unroll 1
-                for (int c = 0; c < BT; c += 16) {
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(taddr + c, r);
-                    tmem_ld_wait();
+            for (int c = 0; c < BT; c += 16) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(taddr + c, r);
+                tmem_ld_wait();
+                if (fetched) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const uint32_t q = sPart[(c + j) * 128 + nl];
+                        if (INT8_KIND) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + static_cast<int32_t>(q));
+                        else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(q)));
+                    }
+                } else if (split) {
                     for (int cc = c_first; cc <= c_last; ++cc) {
                         const uint32_t* part = ws + static_cast<size_t>(cc) * BT * 128;
 #pragma unroll
@@ -1553,17 +1564,80 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(q)));
                         }
                     }
-                    emit(c, r);
+                }
+                // values first, then stores (branches hoisted out of the row loops:
+                // with a type switch per row the rows ran one after another,
+                // ~80 ns each on B200)
+                uint32_t bits[16];  // output elements, low esize bytes
+                if (INT8_KIND && odt == NQ_S32) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bits[j] = r[j];
+                } else {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float a = INT8_KIND ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+                        v[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(a, ep.alpha), sRs[c + j]), cs), bs);
+                    }
+                    if (odt == NQ_BF16) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 2) {
+                            const uint32_t p2 = f32x2_to_bf16x2(v[j], v[j + 1]);
+                            bits[j] = p2 & 0xFFFFu;
+                            bits[j + 1] = p2 >> 16;
+                        }
+                    } else if (odt == NQ_S8) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) bits[j] = static_cast<uint32_t>(static_cast<uint8_t>(requant_s8(v[j])));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) bits[j] = __float_as_uint(v[j]);
+                    }
+                }
+                if (tma_out) {
+                    // [token][row] in the output type; the bulk store clips t >= M, n >= N
+                    if (esize == 2) {
+                        uint16_t* o = reinterpret_cast<uint16_t*>(sOut) + c * 128 + nl;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) o[j * 128] = static_cast<uint16_t>(bits[j]);
+                    } else if (esize == 1) {
+                        uint8_t* o = sOut + c * 128 + nl;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) o[j * 128] = static_cast<uint8_t>(bits[j]);
+                    } else {
+                        uint32_t* o = sOut32 + c * 128 + nl;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) o[j * 128] = bits[j];
+                    }
+                } else if (n < N) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int t = c + j;
+                        if (t < M) {
+                            const size_t o = static_cast<size_t>(t) * ep.ldo + n;
+                            if (esize == 2) static_cast<uint16_t*>(ep.out)[o] = static_cast<uint16_t>(bits[j]);
+                            else if (esize == 1) static_cast<uint8_t*>(ep.out)[o] = static_cast<uint8_t>(bits[j]);
+                            else static_cast<uint32_t*>(ep.out)[o] = bits[j];
+                        }
+                    }
                 }
             }
-            // each parked part has exactly one reader (a CTA parks at most the
-            // first segment of its range): clear its flags for the next launch
-            if (lane == 0)
-                for (int cc = c_first; cc <= c_last; ++cc) flags[cc * 4 + quarter] = 0u;
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+            if (tma_out) fence_proxy_async_smem();
+            named_bar_sync(1, 128);
+            if (tma_out && issuer) {
+                tma_store_2d(&tmO, sOut, slice * 128, 0);
+                bulk_commit_group();
+                bulk_wait_group_read<0>();
+            }
+            // each parked part has exactly one reader (a CTA parks at most the
+            // first segment of its range): clear its flag for the next launch
+            if (issuer)
+                for (int cc = c_first; cc <= c_last; ++cc) flags[cc * 4] = 0u;
             s0 = s1;
         }
+        if (issuer) bulk_wait_group<0>();
     }
     __syncwarp();
     __syncthreads();
@@ -1836,12 +1910,32 @@ template <bool I8, bool KN, int BT>
 nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                              const DeviceInfo& di) {
     using Cfg = DecodeCfg<BT>;
-    CUtensorMap mw, mx;
+    CUtensorMap mw, mx, mo;
     // weights (the GEMM's B) are the MMA's A operand, tokens (the GEMM's A) its B operand
     nq_status_t st = KN ? make_map(&mw, b, d.n, d.k, d.n, 128, BK) : make_map(&mw, b, d.k, d.n, d.k, BK, 128);
     if (st != NQ_SUCCESS) return st;
     st = make_map(&mx, a, d.k, d.m, d.k, BK, BT);
     if (st != NQ_SUCCESS) return st;
+    // outputs leave as one 128 x BT box per slice when the TMA can address them
+    const int esize = d.out_dtype == NQ_BF16 ? 2 : (d.out_dtype == NQ_S8 ? 1 : 4);
+    const bool tma_out = (reinterpret_cast<uintptr_t>(ep.out) % 16) == 0 && (static_cast<size_t>(ep.ldo) * esize) % 16 == 0;
+    std::memset(&mo, 0, sizeof(mo));
+    if (tma_out) {
+        EncodeTiledFn fn;
+        st = get_encode_fn(&fn);
+        if (st != NQ_SUCCESS) return st;
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.n), static_cast<cuuint64_t>(d.m)};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(ep.ldo) * esize};
+        cuuint32_t box[2] = {128, static_cast<cuuint32_t>(BT)};
+        cuuint32_t estr[2] = {1, 1};
+        const CUtensorMapDataType dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                     : esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                  : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+        CUresult r = fn(&mo, dt, 2, ep.out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(NQ_ERROR_CUDA, "cuTensorMapEncodeTiled (decode output) failed (" + std::to_string(int(r)) + ")");
+    }
     const uint32_t idesc = I8 ? make_idesc(2u, 1u, 1u, 0u, 128u, BT, KN ? 1u : 0u)
                               : make_idesc(1u, d.b_format == NQ_E5M2 ? 1u : 0u, d.a_format == NQ_E5M2 ? 1u : 0u, 0u,
                                            128u, BT, KN ? 1u : 0u);
@@ -1851,10 +1945,10 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
     if (st != NQ_SUCCESS) return st;
     const long long total = static_cast<long long>((d.n + 127) / 128) * ((d.k + BK - 1) / BK);
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(total, di.sm_count)));
-    // per CTA one parked partial (BT x 128 accumulators) and four flags (one per
-    // epilogue warp), taken from the stream's flag words, which every launch
-    // leaves cleared: no memset on the launch path
-    const size_t ws_bytes = static_cast<size_t>(grid) * BT * 128 * 4;
+    // per CTA one parked part (BT x 128 accumulators) and one flag (stride 4),
+    // taken from the stream's flag words, which every launch leaves cleared: no
+    // memset on the launch path
+    const size_t ws_bytes = static_cast<size_t>(grid) * Cfg::OUT_BYTES;
     const size_t fl_bytes = static_cast<size_t>(grid) * 4 * 4;
     uint32_t* flags = nullptr;
     st = stream_flags(&flags, grid * 4, s);
@@ -1869,8 +1963,8 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
         e = cudaMemsetAsync(flags, 0, fl_bytes, s);
     }
     if (e == cudaSuccess) {
-        kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(mw, mx, d.m, d.n, d.k, idesc, ep, static_cast<uint32_t*>(ws), flags,
-                                                    device_error_word());
+        kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(mw, mx, mo, tma_out ? 1 : 0, d.m, d.n, d.k, idesc, ep,
+                                                    static_cast<uint32_t*>(ws), flags, device_error_word());
         e = cudaGetLastError();
     }
     scratch_free(ws, s);
@@ -1881,15 +1975,14 @@ template <bool I8, bool KN>
 nq_status_t launch_decode(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                           const DeviceInfo& di) {
     if (d.m <= 16) return launch_decode_bt<I8, KN, 16>(d, a, b, ep, s, di);
-    return launch_decode_bt<I8, KN, 32>(d, a, b, ep, s, di);
+    if (d.m <= 32) return launch_decode_bt<I8, KN, 32>(d, a, b, ep, s, di);
+    return launch_decode_bt<I8, KN, 64>(d, a, b, ep, s, di);
 }
 
 // Few tokens against a large weight: too few output tiles to fill the SMs.
-// Measured on B200 (K=8192, N=28672): the swapped stream-K path streams the
-// weights faster up to 32 tokens; from 64 tokens on, re-reading the token
-// tile for every weight slice costs more than it saves.
+// Up to 64 tokens the swapped stream-K path streams the weights to all SMs.
 bool use_decode(const nq_gemm_desc_t& d, int sm_count) {
-    if (d.m > 32) return false;
+    if (d.m > 64) return false;
     const long long tiles = static_cast<long long>((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
     return tiles < 2LL * sm_count && static_cast<long long>(d.n) * d.k >= (16LL << 20);
 }

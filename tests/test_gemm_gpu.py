@@ -286,7 +286,35 @@ def test_decode_int8_exact_vs_oracle(nq, m, b_layout):
     np.testing.assert_array_equal(got, O.epilogue(acc, True, 1.0, rs, cs))
 
 
-@pytest.mark.parametrize("m", [16, 32, 256])
+@pytest.mark.parametrize("m", [5, 33, 64])
+@pytest.mark.parametrize("n", [4096, 4100])
+def test_decode_every_output_type(nq, m, n):
+    """The decode path for each output type: int32 exact, fp32 and bf16 (with
+    row / column scales and bias) bit-identical to the oracle epilogue, int8
+    equal to QuantizedMatmul::forward.  Outputs leave through a bulk tensor
+    store when a row is a multiple of 16 bytes; n = 4100 makes bf16 and int8
+    rows that are not, so the per-thread store path runs as well, and leaves
+    a last weight slice of 4 rows."""
+    import oracle_lib as O
+    k = 4096
+    a, b = int8_operand((m, k), 21), int8_operand((k, n), 22)
+    acc = O.gemm_i8_acc(a, b, True)
+    np.testing.assert_array_equal(run_gemm(nq, a, b, m, n, k, 2, 2, 0, 2), acc)
+    rng = np.random.default_rng(23)
+    rs = (rng.random(m) * 0.01 + 1e-3).astype(np.float32)
+    cs = (rng.random(n) * 0.01 + 1e-3).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    for out_dtype, bf in ((0, False), (1, True)):
+        got = run_gemm(nq, a, b, m, n, k, 2, 2, 0, out_dtype, 0.5, rs, cs, bias)
+        np.testing.assert_array_equal(got, O.epilogue(acc, bf, 0.5, rs, cs, bias))
+    sa, sb = 0.01, 0.02
+    got = run_gemm(nq, a, b, m, n, k, 2, 2, 0, 3, float(np.float32(sa) * np.float32(sb)))
+    exp = np.empty((m, n), np.int8)
+    O.lib.orc_quantized_matmul(O.ptr(a), O.ptr(b), O.ptr(exp), m, k, n, sa, sb)
+    np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("m", [16, 32, 64, 256])
 def test_decode_fp8_vs_oracle(nq, m):
     import oracle_lib as O
     n, k = 4096, 4096
