@@ -26,6 +26,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "codec.cuh"
 #include "nq_internal.h"
@@ -1382,6 +1383,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     decode_later_ctas(total, G, b1, static_cast<long long>(last_slice + 1) * kblocks, &lc_first, &lc_last);
     const bool last_fetch = (last_s0 % kblocks) == 0 && lc_last == lc_first;  // one later part: bulk-fetched
 
+    // Launched with programmatic stream serialization: the next kernel of the
+    // stream may start its prologue as this grid's CTAs finish.  Everything up
+    // to pdl_wait() touches no memory an earlier kernel may still write (the
+    // weight prefetch only fills L2, which is coherent).
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < D_STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -1399,11 +1405,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
         if (tma_out) tma_prefetch_desc(&tmO);
+        // this CTA's first weight tiles, into L2 while an earlier kernel finishes
+        for (long long kl = b0; kl < b1 && kl < b0 + D_STAGES; ++kl) {
+            const int slice = static_cast<int>(kl / kblocks), kb = static_cast<int>(kl % kblocks);
+            if (W_KN) tma_prefetch_l2_2d(&tmW, slice * 128, kb * BK);
+            else tma_prefetch_l2_2d(&tmW, kb * BK, slice * 128);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, Cfg::TMEM);
         tmem_relinquish();
     }
+    pdl_wait();
     if (threadIdx.x >= 64 && threadIdx.x < 64 + BT) {
         const int t = threadIdx.x - 64;
         sRs[t] = (ep.row_scale && t < M) ? __ldg(ep.row_scale + t) : 1.0f;
@@ -1906,6 +1919,23 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
 }
 
+// Launch with programmatic stream serialization (the kernel triggers its
+// dependents early and waits for its predecessors with griddepcontrol).
+template <class... P, class... A>
+cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+}
+
 template <bool I8, bool KN, int BT>
 nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void* b, const Epi& ep, cudaStream_t s,
                              const DeviceInfo& di) {
@@ -1963,9 +1993,8 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
         e = cudaMemsetAsync(flags, 0, fl_bytes, s);
     }
     if (e == cudaSuccess) {
-        kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(mw, mx, mo, tma_out ? 1 : 0, d.m, d.n, d.k, idesc, ep,
-                                                    static_cast<uint32_t*>(ws), flags, device_error_word());
-        e = cudaGetLastError();
+        e = launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), Cfg::SMEM, s, mw, mx, mo, tma_out ? 1 : 0, d.m, d.n, d.k,
+                       idesc, ep, static_cast<uint32_t*>(ws), flags, device_error_word());
     }
     scratch_free(ws, s);
     return cuda_status(e, "nq_gemm (decode)");

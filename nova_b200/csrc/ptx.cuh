@@ -126,9 +126,23 @@ __device__ __forceinline__ void multimem_red_add_release(uint32_t* mc, uint32_t 
     asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+// Lets the next kernel of the stream (launched with programmatic stream
+// serialization) start its prologue on SMs this grid frees.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the grids this one depends on have completed and their memory
+// operations are visible (returns at once for an ordinary launch).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- TMA ---------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// Brings the box at (x, y) into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
 }
 // 2-D tiled load of the box at (x = inner coordinate, y) into smem; completes
 // `bytes` of transaction count on `bar`.  No cluster multicast.
