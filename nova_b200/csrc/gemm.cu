@@ -875,6 +875,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     const int n_whole = sched_whole(sk, cluster, nclusters);
     const int n_items = sched_items(sk, kblocks, cluster, nclusters);
 
+    // With programmatic stream serialization the next kernel may start its
+    // prologue as this grid's CTAs finish; up to pdl_wait() nothing here reads
+    // or writes memory an earlier kernel may still write (the weight prefetch
+    // only fills L2, which is coherent).
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -893,6 +898,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         tma_prefetch_desc(&tmB);
         if (sk.half_tiles) tma_prefetch_desc(&tmBh);
         if (OUTK != 2) tma_prefetch_desc(&tmC);
+        if (n_items > 0) {
+            // this CTA's B tiles of its first stages, into L2
+            const Unit u0 = sched_unit(sk, kblocks, cluster, nclusters, n_whole, 0);
+            if (!u0.half) {
+                int mb0, nb0;
+                tile_coords(u0.tile, m_tiles, n_tiles, mb0, nb0);
+                for (int kb = u0.kb0; kb < u0.kb1 && kb < u0.kb0 + P_STAGES; ++kb) {
+                    if (B_KN) tma_prefetch_l2_2d(&tmB, nb0 * P_BN + rank * 128, kb * BK);
+                    else tma_prefetch_l2_2d(&tmB, kb * BK, nb0 * P_BN + rank * 128);
+                }
+            }
+        }
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -902,6 +919,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();
     if constexpr (QA) {
         // phase 1a through the operand ring and staging slots, then hand them
         // to TMA: the generic reads of this shared memory come before the
@@ -1036,11 +1054,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             const int tile = un.tile;
             const int acc = it & 1;
             const uint32_t acc_phase = (static_cast<uint32_t>(it) >> 1) & 1u;
+            int mb, nb;
+            tile_coords(tile, m_tiles, n_tiles, mb, nb);
+            // This unit's column operands (and row scale), requested before its
+            // accumulator is ready: while the SMs stream operands, a global load
+            // issued at the chunk that needs it waits about a microsecond (B200).
+            ColOps cops[4];
+            if constexpr (SWIGLU) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    cops[c] = col_ops(ep.col_scale, ep.bias, nb * P_BN + colh * 64 + c * 32, lane, N);
+                    cops[2 + c] = col_ops(ep.col_scale, ep.bias, nb * P_BN + colh * 64 + c * 32 + 128, lane, N);
+                }
+            } else {
+                const int cw0 = un.half ? 64 : 128;
+                const int cb0 = nb * P_BN + (un.half ? (un.half - 1) * 128 : 0) + colh * cw0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) cops[c] = col_ops(ep.col_scale, ep.bias, cb0 + c * 32, lane, N);
+            }
+            const int row_pre = mb * P_BM + row_in_tile;
+            const float rs_pre = (!QA && ep.row_scale && row_pre < M) ? __ldg(ep.row_scale + row_pre) : 1.0f;
+            const bool fixup = !un.park && un.c_first <= un.c_last;
+            if (fixup) {
+                // wait (bounded) until the later parts' 16 warps have parked
+                if (lane == 0)
+                    for (int cc = un.c_first; cc <= un.c_last; ++cc) wait_flag_geq(sk.flags + cc, 2u * P_EPI_WARPS, err);
+                __syncwarp();
+            }
             bool ok = mbar_wait(&tfull[acc], acc_phase, err);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            int mb, nb;
-            tile_coords(tile, m_tiles, n_tiles, mb, nb);
             if constexpr (QA) {
                 // the row scales of this tile come from phase 1 of this launch
                 const int part = (mb + 1) * P_BM > qa.head ? 1 : 0;
@@ -1080,20 +1123,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 }
                 continue;
             }
-            const bool fixup = un.c_first <= un.c_last;
-            if (fixup) {
-                // wait (bounded) until the later parts' 16 warps have parked
-                if (lane == 0)
-                    for (int cc = un.c_first; cc <= un.c_last; ++cc) wait_flag_geq(sk.flags + cc, 2u * P_EPI_WARPS, err);
-                __syncwarp();
-            }
             const int row0_warp = mb * P_BM + static_cast<int>(rank) * 128 + quarter * 32;
             float rs;
             if constexpr (QA) {
                 // the row scales come from phase 1 of this launch (acquired at the top)
                 rs = row < M ? __ldcg(qa.scales + row) : 1.0f;
             } else {
-                rs = (ep.row_scale && row < M) ? __ldg(ep.row_scale + row) : 1.0f;
+                rs = rs_pre;
             }
             if constexpr (SWIGLU) {
                 // this warp's 64 output columns: gate TMEM columns colh*64 + [0,64),
@@ -1116,8 +1152,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                     const int gcol0 = nb * P_BN + colh * 64 + c * 32;
                     const int hcol0 = nb * (P_BN / 2) + colh * 64 + c * 32;
                     if (row0_warp >= M) continue;
-                    const ColOps gop = col_ops(ep.col_scale, ep.bias, gcol0, lane, N);
-                    const ColOps uop = col_ops(ep.col_scale, ep.bias, gcol0 + 128, lane, N);
+                    const ColOps gop = c == 0 ? cops[0] : cops[1];
+                    const ColOps uop = c == 0 ? cops[2] : cops[3];
+                    (void)gcol0;
                     uint8_t* slot = slots + (chunk_seq & 1) * P_EPI_SLOT;
                     if (lane == 0) bulk_wait_group_read<1>();
                     __syncwarp();
@@ -1160,12 +1197,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
             int tile_groups = 0;  // bulk store groups this warp commits for this tile
             // this warp's 128 columns, 32 per tcgen05.ld, the next 32 in flight
             uint32_t r[32];
-            uint4 w[8];  // the first parked part's next chunk, loaded one chunk ahead
-            const uint4* p0 = fixup ? park_slot(sk.ws, un.c_first, w16) : nullptr;
+            // A unit with a fixup is the last of this cluster's range: every MMA
+            // (of both CTAs) is complete, so the operand ring is idle and takes
+            // this warp's 16 KB of the first parked part in one burst of
+            // cp.async, instead of a load latency per chunk.
+            const uint4* sp0 = reinterpret_cast<const uint4*>(smem) + static_cast<size_t>(warp - 2) * (4 * 8 * 32);
+            if (fixup) {
+                const uint4* p0 = park_slot(sk.ws, un.c_first, w16);
+#pragma unroll 4
+                for (int i = 0; i < 4 * 8; ++i) cp_async_16(const_cast<uint4*>(sp0) + i * 32 + lane, p0 + i * 32 + lane);
+                cp_async_commit();
+            }
             tmem_ld_32x32b_x32(taddr, r);
             if (fixup) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) w[q] = __ldcg(p0 + q * 32 + lane);
+                cp_async_wait<0>();
+                __syncwarp();
             }
 #pragma unroll 1
             for (int c = 0; c < nchunks; ++c) {
@@ -1185,16 +1231,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                     }
                 }
                 if (fixup) {
-                    // the parked parts, in cluster order (own part first)
-                    add_parked<INT8_KIND>(cur, w);
+                    // the parked parts, in cluster order
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) add_parked4<INT8_KIND>(cur, q, sp0[(c * 8 + q) * 32 + lane]);
                     for (int cc = un.c_first + 1; cc <= un.c_last; ++cc) {
                         const uint4* pc = park_slot(sk.ws, cc, w16) + c * 8 * 32;
 #pragma unroll
                         for (int q = 0; q < 8; ++q) add_parked4<INT8_KIND>(cur, q, __ldcg(pc + q * 32 + lane));
-                    }
-                    if (c + 1 < nchunks) {
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) w[q] = __ldcg(p0 + ((c + 1) * 8 + q) * 32 + lane);
                     }
                 }
                 const int col0 = col_base + c * 32;
@@ -1206,7 +1249,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
                 uint8_t* slot = slots + (chunk_seq & 1) * P_EPI_SLOT;
                 if (lane == 0) bulk_wait_group_read<1>();  // the store issued two chunks ago has read this slot
                 __syncwarp();
-                const ColOps cop = col_ops(ep.col_scale, ep.bias, col0, lane, N);
+                const ColOps cop = c == 0 ? cops[0] : (c == 1 ? cops[1] : (c == 2 ? cops[2] : cops[3]));
                 // without column scales and bias the per-column operands are
                 // the identities, and skipping them (and their shuffles) gives
                 // the same bits; the branch is warp-uniform
@@ -1802,6 +1845,8 @@ nq_status_t make_out_map(CUtensorMap* map, void* out, const nq_gemm_desc_t& d) {
 StreamK plan_stream_k(int tiles, int kblocks, int clusters, bool allowed) {
     StreamK p{tiles, 0, nullptr, nullptr, 0};
     if (!allowed || clusters < 2 || kblocks < 48 || tiles % clusters == 0) return p;
+    // (measured: also with fewer than two waves -- M = 256, N = 28672, K = 8192,
+    // 112 tiles on 74 clusters -- whole tiles are 3-6 us faster)
     if (tiles % clusters > clusters / 2) return p;
     const int waves = tiles / clusters;
     const int dp = waves >= 2 ? (waves - 1) * clusters : 0;
@@ -1912,28 +1957,19 @@ nq_status_t launch_tc2(const nq_gemm_desc_t& d, const void* a, const void* b, vo
     ArParams ar;
     if (arp) ar = *arp;
     else std::memset(&ar, 0, sizeof(ar));
-    kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mbh, mc, d.m, d.n, d.k, idesc, idesc_h, ep, sk, ar, qa, err);
-    cudaError_t e = cudaGetLastError();
+    // the fused all-reduce launches keep plain stream order (their kernels wait
+    // on other GPUs); the others overlap their prologue with the previous kernel
+    cudaError_t e = cudaSuccess;
+    if (AR) {
+        kern<<<grid, threads, P_SMEM_BYTES, s>>>(ma, mb, mbh, mc, d.m, d.n, d.k, idesc, idesc_h, ep, sk, ar, qa, err);
+        e = cudaGetLastError();
+    } else {
+        e = launch_pdl(kern, dim3(grid), dim3(threads), P_SMEM_BYTES, s, ma, mb, mbh, mc, d.m, d.n, d.k, idesc, idesc_h, ep,
+                       sk, ar, qa, err);
+    }
     if (scratch) scratch_free(scratch, s);
     if (qa_flags) scratch_free(qa_flags, s);
     return cuda_status(e, "nq_gemm (tcgen05, CTA pair)");
-}
-
-// Launch with programmatic stream serialization (the kernel triggers its
-// dependents early and waits for its predecessors with griddepcontrol).
-template <class... P, class... A>
-cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
 }
 
 template <bool I8, bool KN, int BT>

@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/nova_q.h"
 
@@ -26,6 +27,25 @@ struct DeviceInfo {
 };
 // Properties of the current device (cached per device).
 nq_status_t current_device(DeviceInfo* out);
+
+// Launch with programmatic stream serialization: the kernel triggers its
+// dependents early (griddepcontrol.launch_dependents) and waits for its
+// predecessors (griddepcontrol.wait) before it touches memory they may write,
+// so its prologue overlaps the previous kernel's tail.
+template <class... P, class... A>
+cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+}
 
 // Stream-ordered scratch from a library-owned memory pool of the current
 // device: cudaMallocAsync after the first call on a device reuses the pool's

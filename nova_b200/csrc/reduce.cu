@@ -265,11 +265,13 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows_bulk(const In* __restri
     const uint32_t rb = static_cast<uint32_t>(cols) * sizeof(In);
     uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + static_cast<size_t>(stages) * rb);
     const int nv = cols / EPV;
+    dev::pdl_launch_dependents();  // launched with programmatic stream serialization
     if (threadIdx.x == 0) {
         for (int k = 0; k < stages; ++k) dev::mbar_init(&full[k], 1);
         dev::fence_mbar_init();
     }
     __syncthreads();
+    dev::pdl_wait();  // the rows may come from the previous kernel
     const char* base = reinterpret_cast<const char*>(src);
     auto row_of = [&](int i) { return static_cast<long long>(blockIdx.x) + static_cast<long long>(i) * gridDim.x; };
     auto issue = [&](int i) {
@@ -337,11 +339,13 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows_warp(const In* __restri
     uint8_t* ring = q_smem + static_cast<size_t>(warp) * stages * rb;
     uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + static_cast<size_t>(kWarps) * stages * rb) + warp * stages;
     const int nv = cols / EPV;
+    dev::pdl_launch_dependents();  // launched with programmatic stream serialization
     if (lane == 0) {
         for (int k = 0; k < stages; ++k) dev::mbar_init(&full[k], 1);
         dev::fence_mbar_init();
     }
     __syncwarp();
+    dev::pdl_wait();  // the rows may come from the previous kernel
     const long long gw = static_cast<long long>(blockIdx.x) * kWarps + warp;
     const long long nw = static_cast<long long>(gridDim.x) * kWarps;
     const char* base = reinterpret_cast<const char*>(src);
@@ -460,8 +464,9 @@ nq_status_t launch_quant_rows_bulk(const void* src, nq_dtype_t dt, uint8_t* dst,
             per_sm = 1;
         }
         const int grid = static_cast<int>(std::min<long long>(rows, static_cast<long long>(di.sm_count) * per_sm));
-        kern<<<grid, kThreads, smem, s>>>(typed_src, dst, scales, rows, cols, stages, device_error_word());
-        NQ_LAUNCH_CHECK("nq_quantize_rows (bulk)");
+        NQ_CHECK_CUDA(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, typed_src, dst, scales, rows, cols, stages,
+                                 device_error_word()),
+                      "nq_quantize_rows (bulk)");
         return NQ_SUCCESS;
     };
     if (dt == NQ_F32) return launch(k_quant_rows_bulk<F, float>, static_cast<const float*>(src));
@@ -495,8 +500,9 @@ nq_status_t launch_quant_rows_warp(const void* src, nq_dtype_t dt, uint8_t* dst,
         }
         const long long want = (static_cast<long long>(rows) + warps - 1) / warps;
         const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, static_cast<long long>(di.sm_count) * per_sm)));
-        kern<<<grid, kThreads, smem, s>>>(typed_src, dst, scales, rows, cols, stages, device_error_word());
-        NQ_LAUNCH_CHECK("nq_quantize_rows (warp)");
+        NQ_CHECK_CUDA(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, typed_src, dst, scales, rows, cols, stages,
+                                 device_error_word()),
+                      "nq_quantize_rows (warp)");
         return NQ_SUCCESS;
     };
     if (dt == NQ_F32) return launch(k_quant_rows_warp<F, float>, static_cast<const float*>(src));
