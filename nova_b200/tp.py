@@ -448,12 +448,13 @@ class TensorParallelMLP:
         self.H, self.I = hidden_dim, intermediate_size
         self.I_local = intermediate_size // self.tp
         # token chunks of the GEMM / all-reduce pipeline (an explicit value is
-        # always honoured): 1 up to tp = 2, where the fused all-reduce hides
-        # inside the single down GEMM; 4 from tp = 4, where the all-reduce
+        # always honoured): 1 up to tp = 4, where the fused all-reduce hides
+        # inside the single down GEMM; 3 from tp = 8, where the all-reduce
         # outgrows the down GEMM and chunk c's reduction runs inside chunk
-        # c+1's gate/up GEMM (measured at tp = 8: 1.75 ms with 1 chunk, 1.56
-        # with 2 or 4, 1.78 with 8, T = 16384, H = 8192, I = 28672)
-        self.chunks = chunks if chunks is not None else (1 if self.tp <= 2 else 4)
+        # c+1's gate/up GEMM.  Measured on B200, T = 16384, H = 8192,
+        # I = 28672: tp = 4 2.16 ms with 1 chunk, 2.23 with 2, 2.27 with 3 or
+        # 4; tp = 8 1.32 ms with 3 chunks, 1.36 with 2, 1.36-1.40 with 4.
+        self.chunks = chunks if chunks is not None else (1 if self.tp <= 4 else 3)
         # chunk_rows: tokens per chunk (a multiple of 256; the last chunk takes
         # the remainder) instead of `chunks` equal chunks; "plan": plan_chunks'
         # model of the pipeline
