@@ -524,7 +524,7 @@ def _time_batch(fn, reps):
     return e0.elapsed_time(e1) / reps
 
 
-def c3_c4_bench(pk, reps=20):
+def c3_c4_bench(pk, reps=20, c3=True, c4_ms=(16, 64, 256)):
     """BASELINE configs[2] and [3] on one GPU.
     C3, W8A8 FP8 MLP up-projection: X 8192 x 4096 bf16 ~N(0,1) with 41 of
     4096 channels x20; W 4096 x 14336 ~N(0,0.02), per-output-channel E4M3
@@ -545,48 +545,49 @@ def c3_c4_bench(pk, reps=20):
     fp8_peak = 2.0 * pk["bf16_tflops"]
     res = {}
     g = torch.Generator(device="cuda").manual_seed(4)
-    Mx, Kx, Nx = 8192, 4096, 14336
-    x = torch.randn(Mx, Kx, device="cuda", generator=g)
-    out_ch = torch.randperm(Kx, generator=torch.Generator().manual_seed(5))[:41].cuda()
-    x[:, out_ch] *= 20.0
-    x = x.to(torch.bfloat16)
-    w = torch.randn(Kx, Nx, device="cuda", generator=g).mul_(0.02)
-    wq = torch.empty(Kx, Nx, dtype=torch.uint8, device="cuda")
-    ws = torch.empty(Nx, device="cuda")
-    nq.quantize_cols(w.data_ptr(), wq.data_ptr(), ws.data_ptr(), Kx, Nx, nq.E4M3, s)
-    del w
-    xq = torch.empty(Mx, Kx, dtype=torch.uint8, device="cuda")
-    xs = torch.empty(Mx, device="cuda")
-    y = torch.empty(Mx, Nx, dtype=torch.bfloat16, device="cuda")
-    d = nq.make_desc(Mx, Nx, Kx, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, xs.data_ptr(), ws.data_ptr(), 0)
-    quant = lambda: nq.quantize_rows(x.data_ptr(), nq.BF16, xq.data_ptr(), xs.data_ptr(), Mx, Kx, nq.E4M3, s)
-    gemm = lambda: nq.gemm(d, xq.data_ptr(), wq.data_ptr(), y.data_ptr(), s)
-    dq = nq.make_desc(Mx, Nx, Kx, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, 0, ws.data_ptr(), 0)
-    fused = lambda: nq.gemm_quant_a(dq, x.data_ptr(), xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), y.data_ptr(), s)
-    flop = 2.0 * Mx * Nx * Kx
-    # the variants alternate (3 rounds, best of each), so that clock and power
-    # drift over the run does not favour the one measured first
-    t_q = t_g = t_all = t_f = float("inf")
-    for _ in range(3):
-        t_f = min(t_f, _time_flushed(fused, reps, flush))
-        t_all = min(t_all, _time_flushed(lambda: (quant(), gemm()), reps, flush))
-        t_q = min(t_q, _time_flushed(quant, reps, flush))
-        t_g = min(t_g, _time_flushed(gemm, reps, flush))
-    res["c3_w8a8_up_proj"] = {
-        "m": Mx, "k": Kx, "n": Nx,
-        "layer_us": round(t_f * 1e3, 1), "layer_tflops": round(flop / (t_f * 1e-3) / 1e12, 1),
-        "layer_frac_fp8_peak": round(flop / (t_f * 1e-3) / 1e12 / fp8_peak, 3),
-        "layer": "nq_gemm_quant_a: per-token quantize fused into the GEMM, one kernel",
-        "two_launch_layer_us": round(t_all * 1e3, 1), "per_token_quant_us": round(t_q * 1e3, 1),
-        "per_token_quant_GBps": round((3 * Mx * Kx + 4 * Mx) / (t_q * 1e-3) / 1e9, 1),
-        "gemm_only_us": round(t_g * 1e3, 1), "gemm_only_tflops": round(flop / (t_g * 1e-3) / 1e12, 1)}
-    del x, xq, y, wq
-    torch.cuda.empty_cache()
+    if c3:
+        Mx, Kx, Nx = 8192, 4096, 14336
+        x = torch.randn(Mx, Kx, device="cuda", generator=g)
+        out_ch = torch.randperm(Kx, generator=torch.Generator().manual_seed(5))[:41].cuda()
+        x[:, out_ch] *= 20.0
+        x = x.to(torch.bfloat16)
+        w = torch.randn(Kx, Nx, device="cuda", generator=g).mul_(0.02)
+        wq = torch.empty(Kx, Nx, dtype=torch.uint8, device="cuda")
+        ws = torch.empty(Nx, device="cuda")
+        nq.quantize_cols(w.data_ptr(), wq.data_ptr(), ws.data_ptr(), Kx, Nx, nq.E4M3, s)
+        del w
+        xq = torch.empty(Mx, Kx, dtype=torch.uint8, device="cuda")
+        xs = torch.empty(Mx, device="cuda")
+        y = torch.empty(Mx, Nx, dtype=torch.bfloat16, device="cuda")
+        d = nq.make_desc(Mx, Nx, Kx, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, xs.data_ptr(), ws.data_ptr(), 0)
+        quant = lambda: nq.quantize_rows(x.data_ptr(), nq.BF16, xq.data_ptr(), xs.data_ptr(), Mx, Kx, nq.E4M3, s)
+        gemm = lambda: nq.gemm(d, xq.data_ptr(), wq.data_ptr(), y.data_ptr(), s)
+        dq = nq.make_desc(Mx, Nx, Kx, nq.E4M3, nq.E4M3, nq.B_KN, nq.BF16, 1.0, 0, ws.data_ptr(), 0)
+        fused = lambda: nq.gemm_quant_a(dq, x.data_ptr(), xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), y.data_ptr(), s)
+        flop = 2.0 * Mx * Nx * Kx
+        # the variants alternate (3 rounds, best of each), so that clock and power
+        # drift over the run does not favour the one measured first
+        t_q = t_g = t_all = t_f = float("inf")
+        for _ in range(3):
+            t_f = min(t_f, _time_flushed(fused, reps, flush))
+            t_all = min(t_all, _time_flushed(lambda: (quant(), gemm()), reps, flush))
+            t_q = min(t_q, _time_flushed(quant, reps, flush))
+            t_g = min(t_g, _time_flushed(gemm, reps, flush))
+        res["c3_w8a8_up_proj"] = {
+            "m": Mx, "k": Kx, "n": Nx,
+            "layer_us": round(t_f * 1e3, 1), "layer_tflops": round(flop / (t_f * 1e-3) / 1e12, 1),
+            "layer_frac_fp8_peak": round(flop / (t_f * 1e-3) / 1e12 / fp8_peak, 3),
+            "layer": "nq_gemm_quant_a: per-token quantize fused into the GEMM, one kernel",
+            "two_launch_layer_us": round(t_all * 1e3, 1), "per_token_quant_us": round(t_q * 1e3, 1),
+            "per_token_quant_GBps": round((3 * Mx * Kx + 4 * Mx) / (t_q * 1e-3) / 1e9, 1),
+            "gemm_only_us": round(t_g * 1e3, 1), "gemm_only_tflops": round(flop / (t_g * 1e-3) / 1e12, 1)}
+        del x, xq, y, wq
+        torch.cuda.empty_cache()
     Kd, Nd = 8192, 28672
     wi = torch.randint(-127, 128, (Nd, Kd), dtype=torch.int8, device="cuda", generator=g)
     sw = torch.rand(Nd, device="cuda", generator=g).mul_(1e-3)
     c4 = []
-    for Md in (16, 64, 256):
+    for Md in c4_ms:
         xi = torch.randint(-127, 128, (Md, Kd), dtype=torch.int8, device="cuda", generator=g)
         sx = torch.rand(Md, device="cuda", generator=g).mul_(1e-2)
         yo = torch.empty(Md, Nd, dtype=torch.bfloat16, device="cuda")
@@ -831,8 +832,9 @@ def main():
     ap.add_argument("--tp-chunks", type=int, default=None, help="token chunks of the TP pipeline (default: by tp)")
     ap.add_argument("--tp-overlap", choices=["full", "down"], default="full")
     ap.add_argument("--tp-allreduce", choices=["auto", "nvls", "p2p", "nccl"], default="auto")
-    ap.add_argument("--only", choices=["all", "gemm", "sweep", "c3c4"], default="all",
-                    help="gemm: the headline GEMM line alone; sweep / c3c4: one secondary workload alone")
+    ap.add_argument("--c4-m", default="16,64,256", help="decode token counts of the c4 workload")
+    ap.add_argument("--only", choices=["all", "gemm", "sweep", "c3c4", "c4"], default="all",
+                    help="gemm: the headline GEMM line alone; sweep / c3c4 / c4: one secondary workload alone")
     ap.add_argument("--sweep-sizes", default="1048576,58720256,234881024")
     ap.add_argument("--sweep-reps", type=int, default=0)
     args = ap.parse_args()
@@ -840,7 +842,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.only in ("sweep", "c3c4"):
+    if args.only in ("sweep", "c3c4", "c4"):
         # one secondary workload alone (a small, self-contained command for ncu captures)
         import torch
         torch.cuda.set_device(0)
@@ -849,7 +851,7 @@ def main():
             sizes = tuple(int(v) for v in args.sweep_sizes.split(","))
             res = quantize_sweep(pk["hbm_gbs"], sizes, args.sweep_reps)
         else:
-            res = c3_c4_bench(pk)
+            res = c3_c4_bench(pk, c3=args.only == "c3c4", c4_ms=tuple(int(v) for v in args.c4_m.split(",")))
         print(json.dumps({"only": args.only, "result": res}), flush=True)
         return 0
     if args.only == "gemm":
