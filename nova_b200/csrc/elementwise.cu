@@ -119,6 +119,52 @@ __global__ void __launch_bounds__(256) k_quant(const In* __restrict__ src, uint8
     for (size_t i = nvec * 16 + t0; i < n; i += stride) dst[i] = static_cast<uint8_t>(op(load1(src + i)));
 }
 
+// Reference-codec FP8 encode by table.  The code of a float that is not NaN
+// depends only on its sign, exponent and top 7 mantissa bits (bits 31..16): the
+// rounding of fp8_types.hpp:90-95 / :177-186 looks at mantissa bits 22..19
+// (E4M3) or 22..20 (E5M2), the reduced range at bits 22..16 / 22..18.  So a
+// 32 KB table over bits 30..16 in shared memory, ORed with the sign, replaces
+// the ~20 integer operations of dev::compat_e4m3_encode per element (measured
+// on B200 at 224 Mi elements: 71% -> 77% of HBM; a padded, bank-spread table
+// layout was no faster).  Only exponents
+// [LO, HI) need the encoder; below them the code is 0, from HI on 0x7C.  NaN
+// (code 0x7D, no sign) is tested apart, since its low mantissa bits decide it.
+template <int F>
+__global__ void __launch_bounds__(256) k_quant_compat_lut(const float* __restrict__ src, uint8_t* __restrict__ dst,
+                                                          size_t n, int vec) {
+    __shared__ __align__(16) uint8_t lut[32768];
+    constexpr int LO = F == dev::kE4M3 ? 117 : 110;
+    constexpr int HI = F == dev::kE4M3 ? 135 : 143;
+    for (int i = threadIdx.x; i < 32768 / 16; i += blockDim.x) {
+        const int e = i >> 3;  // 16 entries per store, 128 per exponent
+        if (e < LO) reinterpret_cast<uint4*>(lut)[i] = make_uint4(0u, 0u, 0u, 0u);
+        else if (e >= HI) reinterpret_cast<uint4*>(lut)[i] = make_uint4(0x7C7C7C7Cu, 0x7C7C7C7Cu, 0x7C7C7C7Cu, 0x7C7C7C7Cu);
+    }
+    for (int i = threadIdx.x; i < (HI - LO) * 128; i += blockDim.x) {
+        const uint32_t idx = static_cast<uint32_t>(LO * 128 + i);
+        const float v = __uint_as_float(idx << 16);
+        lut[idx] = static_cast<uint8_t>(F == dev::kE4M3 ? dev::compat_e4m3_encode(v) : dev::compat_e5m2_encode(v));
+    }
+    __syncthreads();
+    auto enc = [&](float x) -> uint32_t {
+        const uint32_t u = __float_as_uint(x);
+        const uint32_t c = static_cast<uint32_t>(lut[(u >> 16) & 0x7FFFu]) | ((u >> 24) & 0x80u);
+        return x != x ? 0x7Du : c;
+    };
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t nvec = vec ? n / 16 : 0;
+    for (size_t v = t0; v < nvec; v += stride) {
+        float x[16];
+        load16(src + v * 16, x);
+        uint32_t c[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[i] = enc(x[i]);
+        store16_codes(dst + v * 16, c);
+    }
+    for (size_t i = nvec * 16 + t0; i < n; i += stride) dst[i] = static_cast<uint8_t>(enc(load1(src + i)));
+}
+
 // Scaled OCP / INT8 quantize, the scale read from device memory.
 template <int F, class In>
 __global__ void __launch_bounds__(256) k_quant_scaled(const In* __restrict__ src,
@@ -370,6 +416,29 @@ nq_status_t launch_quant(const In* src, uint8_t* dst, size_t n, Op op, cudaStrea
     return NQ_SUCCESS;
 }
 
+// Tables pay off once every CTA has a few thousand elements to encode.
+constexpr size_t kCompatLutMin = size_t(1) << 22;
+
+template <int F>
+nq_status_t launch_quant_compat(const float* src, uint8_t* dst, size_t n, cudaStream_t s, const char* what) {
+    if (n < kCompatLutMin) {
+        if (F == dev::kE4M3) return launch_quant(src, dst, n, CompatE4M3{}, s, what);
+        return launch_quant(src, dst, n, CompatE5M2{}, s, what);
+    }
+    if (!src || !dst) return fail(NQ_ERROR_INVALID_VALUE, std::string(what) + ": null pointer");
+    DeviceInfo di;
+    nq_status_t st = current_device(&di);
+    if (st != NQ_SUCCESS) return st;
+    int grid;
+    st = grid_for(n, &grid);
+    if (st != NQ_SUCCESS) return st;
+    grid = std::min(grid, di.sm_count * 6);  // 32 KB of table per CTA
+    const int vec = aligned16(src) && aligned16(dst);
+    k_quant_compat_lut<F><<<grid, 256, 0, s>>>(src, dst, n, vec);
+    NQ_LAUNCH_CHECK(what);
+    return NQ_SUCCESS;
+}
+
 template <class Op>
 nq_status_t launch_dequant(const uint8_t* src, float* dst, size_t n, Op op, cudaStream_t s, const char* what) {
     if (n == 0) return NQ_SUCCESS;
@@ -422,10 +491,10 @@ using nq::fail;
 extern "C" {
 
 nq_status_t nq_quantize_f32_to_fp8e4m3(const float* src, uint8_t* dst, size_t n, nq_stream_t s) {
-    return nq::launch_quant(src, dst, n, nq::CompatE4M3{}, s, "nq_quantize_f32_to_fp8e4m3");
+    return nq::launch_quant_compat<nq::dev::kE4M3>(src, dst, n, s, "nq_quantize_f32_to_fp8e4m3");
 }
 nq_status_t nq_quantize_f32_to_fp8e5m2(const float* src, uint8_t* dst, size_t n, nq_stream_t s) {
-    return nq::launch_quant(src, dst, n, nq::CompatE5M2{}, s, "nq_quantize_f32_to_fp8e5m2");
+    return nq::launch_quant_compat<nq::dev::kE5M2>(src, dst, n, s, "nq_quantize_f32_to_fp8e5m2");
 }
 nq_status_t nq_dequantize_fp8e4m3_to_f32(const uint8_t* src, float* dst, size_t n, float scale,
                                          nq_stream_t s) {

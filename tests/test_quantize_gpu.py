@@ -36,6 +36,27 @@ def test_compat_fp8_quantize_bit_exact(nq, n, fmt, off):
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("off", [0, 4])
+def test_compat_fp8_quantize_table_path_every_pattern(nq, fmt, off):
+    """From 4 Mi elements on the reference-codec encode reads a table indexed by
+    the float's bits 30..16 (plus the sign and a NaN test).  Every 16-bit top
+    pattern -- each sign, exponent and top-7 mantissa bits -- with low mantissa
+    bits 0, 1, 0x8000 and 0xFFFF (every NaN form included), repeated past 4 Mi
+    with a ragged tail, must match the oracle bit for bit."""
+    import oracle_lib as O
+    from gpu_util import dev, empty, host, ptr, stream
+    top = np.arange(1 << 16, dtype=np.uint32) << 16
+    low = np.array([0, 1, 0x8000, 0xFFFF], dtype=np.uint32)
+    u = (top[:, None] | low[None, :]).reshape(-1)
+    n = (1 << 22) + 3
+    x = np.tile(u, n // u.size + 1)[:n].view(np.float32)
+    d_x, d_q = dev(x, off), empty(n, off // 4)
+    fn = nq.quantize_f32_to_fp8e4m3 if fmt == 0 else nq.quantize_f32_to_fp8e5m2
+    fn(ptr(d_x), ptr(d_q), n, stream())
+    np.testing.assert_array_equal(host(d_q, np.uint8), O.quantize_compat(x, fmt))
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
 def test_compat_fp8_special_values(nq, fmt):
     import oracle_lib as O
     from gpu_util import dev, empty, host, ptr, stream
