@@ -1392,7 +1392,7 @@ __device__ __forceinline__ void decode_later_ctas(long long total, int G, long l
 template <bool INT8_KIND, bool W_KN, int BT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_decode(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                  const __grid_constant__ CUtensorMap tmO, int tma_out, int M, int N, int K, uint32_t idesc, Epi ep,
+                  const __grid_constant__ CUtensorMap tmO, int M, int N, int K, uint32_t idesc, Epi ep,
                   uint32_t* ws, uint32_t* flags, uint32_t* err) {
     using Cfg = DecodeCfg<BT>;
     constexpr int D_STAGES = Cfg::STAGES;
@@ -1447,7 +1447,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
-        if (tma_out) tma_prefetch_desc(&tmO);
+        tma_prefetch_desc(&tmO);
         // this CTA's first weight tiles, into L2 while an earlier kernel finishes
         for (long long kl = b0; kl < b1 && kl < b0 + D_STAGES; ++kl) {
             const int slice = static_cast<int>(kl / kblocks), kb = static_cast<int>(kl % kblocks);
@@ -1650,7 +1650,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         for (int j = 0; j < 16; ++j) bits[j] = __float_as_uint(v[j]);
                     }
                 }
-                if (tma_out) {
+                {
                     // [token][row] in the output type; the bulk store clips t >= M, n >= N
                     if (esize == 2) {
                         uint16_t* o = reinterpret_cast<uint16_t*>(sOut) + c * 128 + nl;
@@ -1665,24 +1665,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) o[j * 128] = bits[j];
                     }
-                } else if (n < N) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = c + j;
-                        if (t < M) {
-                            const size_t o = static_cast<size_t>(t) * ep.ldo + n;
-                            if (esize == 2) static_cast<uint16_t*>(ep.out)[o] = static_cast<uint16_t>(bits[j]);
-                            else if (esize == 1) static_cast<uint8_t*>(ep.out)[o] = static_cast<uint8_t>(bits[j]);
-                            else static_cast<uint32_t*>(ep.out)[o] = bits[j];
-                        }
-                    }
                 }
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
-            if (tma_out) fence_proxy_async_smem();
+            fence_proxy_async_smem();
             named_bar_sync(1, 128);
-            if (tma_out && issuer) {
+            if (issuer) {
                 tma_store_2d(&tmO, sOut, slice * 128, 0);
                 bulk_commit_group();
                 bulk_wait_group_read<0>();
@@ -1982,11 +1971,12 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
     if (st != NQ_SUCCESS) return st;
     st = make_map(&mx, a, d.k, d.m, d.k, BK, BT);
     if (st != NQ_SUCCESS) return st;
-    // outputs leave as one 128 x BT box per slice when the TMA can address them
+    // outputs leave as one 128 x BT box per slice (nq_gemm takes this path only
+    // with a 16-byte aligned output and N % 16 == 0, so the rows are addressable)
     const int esize = d.out_dtype == NQ_BF16 ? 2 : (d.out_dtype == NQ_S8 ? 1 : 4);
-    const bool tma_out = (reinterpret_cast<uintptr_t>(ep.out) % 16) == 0 && (static_cast<size_t>(ep.ldo) * esize) % 16 == 0;
-    std::memset(&mo, 0, sizeof(mo));
-    if (tma_out) {
+    if ((reinterpret_cast<uintptr_t>(ep.out) % 16) != 0 || (static_cast<size_t>(ep.ldo) * esize) % 16 != 0)
+        return fail(NQ_ERROR_UNSUPPORTED, "nq_gemm (decode): the output must be 16-byte aligned with 16-byte rows");
+    {
         EncodeTiledFn fn;
         st = get_encode_fn(&fn);
         if (st != NQ_SUCCESS) return st;
@@ -2029,8 +2019,8 @@ nq_status_t launch_decode_bt(const nq_gemm_desc_t& d, const void* a, const void*
         e = cudaMemsetAsync(flags, 0, fl_bytes, s);
     }
     if (e == cudaSuccess) {
-        e = launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), Cfg::SMEM, s, mw, mx, mo, tma_out ? 1 : 0, d.m, d.n, d.k,
-                       idesc, ep, static_cast<uint32_t*>(ws), flags, device_error_word());
+        e = launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), Cfg::SMEM, s, mw, mx, mo, d.m, d.n, d.k, idesc, ep,
+                       static_cast<uint32_t*>(ws), flags, device_error_word());
     }
     scratch_free(ws, s);
     return cuda_status(e, "nq_gemm (decode)");

@@ -286,15 +286,30 @@ def test_decode_int8_exact_vs_oracle(nq, m, b_layout):
     np.testing.assert_array_equal(got, O.epilogue(acc, True, 1.0, rs, cs))
 
 
+@pytest.mark.parametrize("m,n,k", [(7, 4112, 4112), (40, 4352, 3856), (64, 4240, 4000)])
+@pytest.mark.parametrize("b_layout", [1, 0])
+def test_decode_ragged_k_and_n(nq, m, n, k, b_layout):
+    """The decode path with K not a multiple of the 128-byte k-block (the last
+    k-block is zero-filled by the TMA) and N not a multiple of the 128-row weight
+    slice: int32 exact, bf16 bit-identical to the oracle epilogue."""
+    import oracle_lib as O
+    a = int8_operand((m, k), 31)
+    b = int8_operand((k, n) if b_layout == 0 else (n, k), 32)
+    acc = O.gemm_i8_acc(a, b, b_layout == 0)
+    np.testing.assert_array_equal(run_gemm(nq, a, b, m, n, k, 2, 2, b_layout, 2), acc)
+    rs = (np.random.default_rng(33).random(m) * 0.01 + 1e-3).astype(np.float32)
+    cs = (np.random.default_rng(34).random(n) * 0.01 + 1e-3).astype(np.float32)
+    got = run_gemm(nq, a, b, m, n, k, 2, 2, b_layout, 1, 1.0, rs, cs)
+    np.testing.assert_array_equal(got, O.epilogue(acc, True, 1.0, rs, cs))
+
+
 @pytest.mark.parametrize("m", [5, 33, 64])
-@pytest.mark.parametrize("n", [4096, 4100])
+@pytest.mark.parametrize("n", [4096, 4112])
 def test_decode_every_output_type(nq, m, n):
     """The decode path for each output type: int32 exact, fp32 and bf16 (with
     row / column scales and bias) bit-identical to the oracle epilogue, int8
-    equal to QuantizedMatmul::forward.  Outputs leave through a bulk tensor
-    store when a row is a multiple of 16 bytes; n = 4100 makes bf16 and int8
-    rows that are not, so the per-thread store path runs as well, and leaves
-    a last weight slice of 4 rows."""
+    equal to QuantizedMatmul::forward; n = 4112 leaves a last weight slice of
+    16 rows, which the bulk output store clips."""
     import oracle_lib as O
     k = 4096
     a, b = int8_operand((m, k), 21), int8_operand((k, n), 22)
