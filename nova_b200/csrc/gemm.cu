@@ -899,15 +899,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AR ? P_THREADS_AR : 
         if (sk.half_tiles) tma_prefetch_desc(&tmBh);
         if (OUTK != 2) tma_prefetch_desc(&tmC);
         if (n_items > 0) {
-            // this CTA's B tiles of its first stages, into L2
+            // this CTA's operand tiles of its first stages, into L2, while the
+            // barriers and TMEM are set up (and, launched after a kernel that
+            // triggers early, while that kernel finishes); A only when it is an
+            // input of the launch
             const Unit u0 = sched_unit(sk, kblocks, cluster, nclusters, n_whole, 0);
-            if (!u0.half) {
-                int mb0, nb0;
-                tile_coords(u0.tile, m_tiles, n_tiles, mb0, nb0);
-                for (int kb = u0.kb0; kb < u0.kb1 && kb < u0.kb0 + P_STAGES; ++kb) {
-                    if (B_KN) tma_prefetch_l2_2d(&tmB, nb0 * P_BN + rank * 128, kb * BK);
-                    else tma_prefetch_l2_2d(&tmB, kb * BK, nb0 * P_BN + rank * 128);
-                }
+            int mb0, nb0;
+            tile_coords(u0.tile, m_tiles, n_tiles, mb0, nb0);
+            for (int kb = u0.kb0; kb < u0.kb1 && kb < u0.kb0 + P_STAGES; ++kb) {
+                if (!QA) tma_prefetch_l2_2d(&tmA, kb * BK, mb0 * P_BM + static_cast<int>(rank) * 128);
+                if (u0.half) continue;
+                if (B_KN) tma_prefetch_l2_2d(&tmB, nb0 * P_BN + rank * 128, kb * BK);
+                else tma_prefetch_l2_2d(&tmB, kb * BK, nb0 * P_BN + rank * 128);
             }
         }
     }
