@@ -47,9 +47,10 @@ def peaks():
     try:
         with open(path) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "source": "measured"}
     except Exception:
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def profile_traffic(name):
@@ -787,6 +788,9 @@ def tp_mlp_bench(world, rank, steps, warmup, T=16384, H=8192, I=28672, chunks=No
                                       else ("nccl" if world > 1 else "none")),
            "chunks": mlp.chunks, "ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3)),
            "tflops_total": round(tflops, 1), "frac_of_tp_x_fp8_peak": round(tflops / (world * fp8_peak), 4),
+           # a forward is milliseconds of back-to-back GEMMs under the 1 kW power cap:
+           # its roofline is the sustained figure (2 x sustained bf16 of MEASURED_PEAKS.json)
+           "frac_of_tp_x_fp8_sustained": round(tflops / (world * 2.0 * pk["bf16_tflops_sustained"]), 4),
            "allreduce_bytes": 2 * T * H if world > 1 else 0, "scaling": "strong"}
     # parity of sampled rows spread over every token chunk, from one more forward
     y = mlp.forward(x, out, 1, T, sync=True)
