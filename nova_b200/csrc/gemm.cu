@@ -2078,21 +2078,48 @@ nq_status_t launch_tc(const nq_gemm_desc_t& d, const void* a, const void* b, con
     return NQ_SUCCESS;
 }
 
-// QuantizedMatmul::mixed_precision (quantize_ops.hpp:83-102): one thread per
-// output, the reference's order and roundings (multiply, then add).
-__global__ void __launch_bounds__(256) k_mixed_precision(const float* __restrict__ a, const int8_t* __restrict__ b,
-                                                         const float* __restrict__ scale_b, float* __restrict__ out,
-                                                         int M, int K, int N) {
-    const int col = blockIdx.x * 64 + (threadIdx.x & 63);
-    const int row = blockIdx.y * 4 + (threadIdx.x >> 6);
-    if (row >= M || col >= N) return;
-    const float* ar = a + static_cast<size_t>(row) * K;
-    float s = 0.0f;
-    for (int p = 0; p < K; ++p) {
-        const float bv = __fmul_rn(static_cast<float>(b[static_cast<size_t>(p) * N + col]), __ldg(scale_b + p));
-        s = __fadd_rn(s, __fmul_rn(__ldg(ar + p), bv));
+// QuantizedMatmul::mixed_precision (quantize_ops.hpp:83-102).  Every output
+// keeps the reference's order and roundings -- for p = 0 .. K-1:
+// s = s + a[i,p] * (float(b[p,j]) * scale[p]), one rounding per multiply and add
+// -- so the sum runs sequentially over K; the parallelism is across outputs.  A
+// thread carries MP_ROWS rows of one column: each weight byte is read and
+// scaled once per MP_ROWS outputs, and the block's activation rows are staged
+// in shared memory ([k][row], two 16-byte reads per k).
+constexpr int MP_ROWS = 8, MP_COLS = 128, MP_KC = 64;
+__global__ void __launch_bounds__(MP_COLS) k_mixed_precision(const float* __restrict__ a, const int8_t* __restrict__ b,
+                                                             const float* __restrict__ scale_b, float* __restrict__ out,
+                                                             int M, int K, int N) {
+    __shared__ __align__(16) float sa[MP_KC][MP_ROWS];
+    const int col = blockIdx.x * MP_COLS + threadIdx.x;
+    const int r0 = blockIdx.y * MP_ROWS;
+    float acc[MP_ROWS];
+#pragma unroll
+    for (int r = 0; r < MP_ROWS; ++r) acc[r] = 0.0f;
+    for (int p0 = 0; p0 < K; p0 += MP_KC) {
+        const int kc = min(MP_KC, K - p0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < MP_KC * MP_ROWS; i += MP_COLS) {
+            const int r = i / MP_KC, p = i % MP_KC;  // consecutive threads: consecutive k of one row
+            sa[p][r] = (r0 + r < M && p < kc) ? __ldg(a + static_cast<size_t>(r0 + r) * K + p0 + p) : 0.0f;
+        }
+        __syncthreads();
+        if (col < N) {
+            for (int p = 0; p < kc; ++p) {
+                const float bv = __fmul_rn(static_cast<float>(b[static_cast<size_t>(p0 + p) * N + col]),
+                                           __ldg(scale_b + p0 + p));
+                const float4 x0 = *reinterpret_cast<const float4*>(&sa[p][0]);
+                const float4 x1 = *reinterpret_cast<const float4*>(&sa[p][4]);
+                const float xs[MP_ROWS] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int r = 0; r < MP_ROWS; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(xs[r], bv));
+            }
+        }
     }
-    out[static_cast<size_t>(row) * N + col] = s;
+    if (col < N) {
+#pragma unroll
+        for (int r = 0; r < MP_ROWS; ++r)
+            if (r0 + r < M) out[static_cast<size_t>(r0 + r) * N + col] = acc[r];
+    }
 }
 
 // Byte transpose (rows x cols -> cols x rows) through 32 x 32 shared tiles,
@@ -2417,9 +2444,9 @@ nq_status_t nq_mixed_precision_matmul(const float* a, const int8_t* b, const flo
     nq::DeviceInfo di;
     nq_status_t st = nq::current_device(&di);
     if (st != NQ_SUCCESS) return st;
-    dim3 grid((n + 63) / 64, (m + 3) / 4);
+    dim3 grid((n + nq::MP_COLS - 1) / nq::MP_COLS, (m + nq::MP_ROWS - 1) / nq::MP_ROWS);
     if (grid.y > 65535) return nq::fail(NQ_ERROR_UNSUPPORTED, "nq_mixed_precision_matmul: M too large");
-    nq::k_mixed_precision<<<grid, 256, 0, s>>>(a, b, scale_b, out, m, k, n);
+    nq::k_mixed_precision<<<grid, nq::MP_COLS, 0, s>>>(a, b, scale_b, out, m, k, n);
     NQ_LAUNCH_CHECK("nq_mixed_precision_matmul");
     return NQ_SUCCESS;
 }

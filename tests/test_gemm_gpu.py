@@ -192,12 +192,13 @@ def test_int8_requant_epilogue_matches_quantized_matmul(nq, m, n, k):
     np.testing.assert_array_equal(got, exp)
 
 
-def test_mixed_precision_matmul(nq):
+@pytest.mark.parametrize("m,k,n", [(37, 300, 70), (1, 64, 1), (9, 1000, 3001), (64, 129, 256)])
+def test_mixed_precision_matmul(nq, m, k, n):
     """QuantizedMatmul::mixed_precision (quantize_ops.hpp:83-102): identical
-    roundings to the reference host loop."""
+    roundings to the reference host loop (rows and columns that fill no whole
+    8 x 128 block, k past one 64-deep stage)."""
     from gpu_util import dev, empty, host, ptr, stream
-    m, k, n = 37, 300, 70
-    rng = np.random.default_rng(9)
+    rng = np.random.default_rng(9 + m + k + n)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = rng.integers(-127, 128, (k, n), dtype=np.int8)
     s = (rng.random(k) * 0.1).astype(np.float32)
