@@ -660,7 +660,9 @@ def tp_parity(mlp, x, y, shards, rows, world, group=None):
         all-reduce; the output itself at tp = 1) within the same bar of an
         fp64 product of the GPU's h codes with the down shard;
       - tp > 1: the reduced output is one bf16 rounding of the exact sum of
-        the ranks' partials (max error 2^-8 of |sum|, floored at 1e-2 rms).
+        the ranks' partials (max error 2^-8 of |sum|, floored at 1e-2 rms);
+        through NVSwitch multicast the switch converts its fp32 sum to bf16
+        itself, within one bf16 ulp (2 x 2^-8) rather than half of one.
     (b) Against an fp32 computation with the UNQUANTIZED weights
         (tensor_parallel_layers.cpp:561-579 in fp32): normwise relative error
         below 0.1 (two E4M3 quantizations of activations and weights, about
@@ -707,6 +709,7 @@ def tp_parity(mlp, x, y, shards, rows, world, group=None):
     part_ref = (hq[idx].view(f8).double() @ dl.q.view(f8).double()) * sh[idx].double()[:, None] * dl.s.double()[None, :]
     fused = mlp.down.fused
     got = y[idx].double()
+    sum_bound = 2.0 if (fused is not None and fused.multicast()) else 1.0
     if world == 1:
         part_err, sum_err = rel(got, part_ref), 0.0
     elif fused is not None:
@@ -742,10 +745,11 @@ def tp_parity(mlp, x, y, shards, rows, world, group=None):
     replicated = bool(torch.equal(mx, mn))
     dev_err, codes_ok = int(worst[0].item()), worst[1].item() == 0.0
     h_err, part_err, sum_err = (float(v) for v in worst[2:].tolist())
-    ok = (codes_ok and h_err <= 1e-2 and part_err <= 1e-2 and sum_err <= 1.0 and fp32_norm <= 0.1 and replicated
-          and dev_err == 0)
+    ok = (codes_ok and h_err <= 1e-2 and part_err <= 1e-2 and sum_err <= sum_bound and fp32_norm <= 0.1
+          and replicated and dev_err == 0)
     return {"ok": ok, "rows": len(rows), "codes_bit_exact": codes_ok, "h_max_rel_err": round(h_err, 6),
             "partial_max_rel_err": round(part_err, 6), "sum_err_in_bf16_roundings": round(sum_err, 4),
+            "sum_err_bound": sum_bound,
             "vs_fp32_weights_norm_err": round(fp32_norm, 5), "replicated": replicated, "device_errors": dev_err}
 
 
