@@ -39,7 +39,8 @@ def test_compat_fp8_quantize_bit_exact(nq, n, fmt, off):
 @pytest.mark.parametrize("off", [0, 4])
 def test_compat_fp8_quantize_table_path_every_pattern(nq, fmt, off):
     """From 4 Mi elements on the reference-codec encode reads a table indexed by
-    the float's bits 30..16 (plus the sign and a NaN test).  Every 16-bit top
+    the float's clamped exponent and top 7 mantissa bits (plus the sign and a
+    NaN test).  Every 16-bit top
     pattern -- each sign, exponent and top-7 mantissa bits -- with low mantissa
     bits 0, 1, 0x8000 and 0xFFFF (every NaN form included), repeated past 4 Mi
     with a ragged tail, must match the oracle bit for bit."""
