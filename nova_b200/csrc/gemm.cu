@@ -1379,8 +1379,9 @@ struct DecodeCfg {
 
 __device__ __forceinline__ long long range_begin(long long total, int c, int G) { return total * c / G; }
 
-// Later CTAs whose ranges touch the slice that starts at k-block s0 and is cut
-// at this CTA's range end b1 (c_first > c_last when none).
+// The later CTAs [c_first, c_last] whose ranges hold the rest of a slice that
+// ends at k-block slice_end, when this CTA's part of it ends at s1 (c_first >
+// c_last when s1 == slice_end: the slice is this CTA's alone from there on).
 __device__ __forceinline__ void decode_later_ctas(long long total, int G, long long s1, long long slice_end, int* c_first,
                                                   int* c_last) {
     *c_first = blockIdx.x + 1;
