@@ -13,7 +13,7 @@ def test_roofline_inputs():
     pk = bench.peaks()
     assert pk["source"] in ("measured", "fallback") and pk["hbm_gbs"] > 1000 and pk["bf16_tflops"] > 500
     # roofline.traffic comes from the committed ncu summary of the headline kernel
-    assert bench.profile_traffic("fp8_gemm_4096.md") == 36235264.0
+    assert bench.profile_traffic("fp8_gemm_4096.md") == 36319488.0
     assert bench.profile_traffic("no_such_profile.md") is None
     assert bench.FLOPS == 2.0 * 4096 ** 3
 
